@@ -1,0 +1,430 @@
+#!/usr/bin/env python
+"""Benchmark of the infengine weight-matmul hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one bs=1 decode token through the weight-matmul path of
+random-init Llama-3.1-8B (bf16, N(0,0.02) weights, fixed seed):
+    32 x [ fused Q/K/V projection + RoPE into the KV cache (position 2047),
+           O projection, FFN gate/up + SwiGLU, FFN down ]
+    + lm_head with the fused greedy argmax.
+15.01 GB of weights are streamed per step (far above the 126 MB L2, so no
+flush is needed). The attention core, RMSNorm and residual adds are not part
+of this path and are not run: every layer's projections read the step's
+hidden state and the O projection reads the Q output as its stand-in for the
+attention output.
+
+Our arm captures the step (129 kernel launches through the C-ABI) in one CUDA
+graph. The reference arm (--impl reference) runs the reference's own code
+for the same path, compiled from its sources for sm_100a (cuBLAS GEMMs,
+its RoPE, SwiGLU and argmax kernels; fp16, the reference's only dtype),
+launched eagerly on the legacy default stream as its decode loop does.
+
+For N > 1 (torchrun) every rank runs a full replica (weak scaling); the
+printed value is the sum over ranks, timed as the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s bs1 & matmul HBM GB/s, prefill GEMM TFLOPS vs B200 roofline"
+H, F, V, L = 4096, 14336, 128256, 32
+NQ, NKV, HD, CTX = 32, 8, 128, 8192
+POS = 2047  # the 2048th token: decode right after a 2048-token prompt
+LAYER_WEIGHT_ELEMS = (NQ + 2 * NKV) * HD * H + H * H + 3 * F * H
+WEIGHT_BYTES = 2 * (L * LAYER_WEIGHT_ELEMS + V * H)
+GATE_UP_BYTES = 2 * (2 * F * H + H + F)  # one gate/up+SwiGLU launch at M=1
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def load_traffic():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("gate_up_swiglu_m1_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+# ------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of this rank's GPU during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(parts)
+            except ValueError:
+                pass
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------- weights
+def make_weights(torch, dev, dtype, seed: int):
+    """Random-init Llama-3.1-8B projection weights: N(0,0.02) drawn in fp32
+    from a seeded generator, rounded to bf16 (then to the arm's dtype)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+
+    def w(*shape):
+        t = torch.randn(*shape, generator=g, device=dev, dtype=torch.float32).mul_(0.02)
+        t = t.to(torch.bfloat16)
+        return t if dtype == torch.bfloat16 else t.to(dtype)
+
+    layers = []
+    for _ in range(L):
+        layers.append({"wq": w(NQ * HD, H), "wk": w(NKV * HD, H), "wv": w(NKV * HD, H), "wo": w(H, H),
+                       "wg": w(F, H), "wu": w(F, H), "wd": w(H, F)})
+    lm = w(V, H)
+    return layers, lm
+
+
+# ---------------------------------------------------------------- our arm
+class OursStep:
+    def __init__(self, torch, dev, seed):
+        import infengine_b200 as ie
+        from infengine_b200.host import rope_tables
+        self.ie, self.torch = ie, torch
+        dt = torch.bfloat16
+        self.layers, self.lm = make_weights(torch, dev, dt, seed)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed + 1)
+        self.x = torch.randn(1, H, generator=g, device=dev, dtype=torch.float32).to(dt)
+        self.q = torch.empty(NQ, 1, HD, device=dev, dtype=dt)
+        self.attn_out = torch.empty(1, H, device=dev, dtype=dt)
+        self.h = torch.empty(1, F, device=dev, dtype=dt)
+        self.ffn_out = torch.empty(1, H, device=dev, dtype=dt)
+        self.kc = torch.zeros(L, NKV, CTX, HD, device=dev, dtype=dt)
+        self.vc = torch.zeros(L, NKV, CTX, HD, device=dev, dtype=dt)
+        cos, sin = rope_tables(CTX)
+        self.cos = torch.from_numpy(cos).to(dev)
+        self.sin = torch.from_numpy(sin).to(dev)
+        self.ws = torch.zeros(ie.lm_head_workspace_bytes(1), dtype=torch.uint8, device=dev)
+        self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.launches_per_step = L * 4 + 1
+
+    def __call__(self):
+        ie = self.ie
+        for l, w in enumerate(self.layers):
+            ie.qkv(self.x, w["wq"], w["wk"], w["wv"], self.q, self.kc[l], self.vc[l], CTX * HD, POS, self.cos,
+                   self.sin)
+            ie.gemm(self.q.view(1, H), w["wo"], self.attn_out)
+            ie.ffn_gate_up(self.x, w["wg"], w["wu"], self.h)
+            ie.gemm(self.h, w["wd"], self.ffn_out)
+        ie.lm_head_argmax(self.x, self.lm, self.ws, idx_out=self.tok)
+
+    def gate_up_only(self):
+        for w in self.layers:
+            self.ie.ffn_gate_up(self.x, w["wg"], w["wu"], self.h)
+
+
+# ---------------------------------------------------------- reference arm
+class RefStep:
+    def __init__(self, torch, dev, seed):
+        sys.path.insert(0, str(ROOT / "tests"))
+        from ref_lib import p, ref
+        from infengine_b200.host import rope_tables
+        self.R, self.p, self.torch = ref(), p, torch
+        dt = torch.float16
+        self.layers, self.lm = make_weights(torch, dev, dt, seed)  # bf16 -> fp16 as model_weights.cu:61-78
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed + 1)
+        self.x = torch.randn(1, H, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16).to(dt)
+        self.q = torch.empty(NQ, 1, HD, device=dev, dtype=dt)
+        self.attn_out = torch.empty(1, H, device=dev, dtype=dt)
+        self.ffn_out = torch.empty(1, H, device=dev, dtype=dt)
+        self.kc = torch.zeros(L, NKV, CTX, HD, device=dev, dtype=dt)
+        self.vc = torch.zeros(L, NKV, CTX, HD, device=dev, dtype=dt)
+        cos, sin = rope_tables(CTX)
+        self.cos = torch.from_numpy(cos).to(dev)
+        self.sin = torch.from_numpy(sin).to(dev)
+        self.ws = torch.empty(self.R.ref_ffn_workspace_size(1), dtype=torch.uint8, device=dev)
+        self.logits = torch.empty(V, device=dev, dtype=dt)
+        self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.R.ref_set_stream(None)  # legacy default stream, as manager.cpp:58-59 leaves it
+        self.launches_per_step = None  # cuBLAS chooses its own kernels
+
+    def __call__(self):
+        R, p = self.R, self.p
+        for l, w in enumerate(self.layers):
+            kdst, vdst = self.kc[l][:, POS], self.vc[l][:, POS]
+            R.ref_qkv_proj(1, p(self.x), p(w["wq"]), p(w["wk"]), p(w["wv"]), p(self.q), p(kdst), p(vdst), NQ, NKV)
+            R.ref_apply_rope(POS, NKV, 1, p(self.cos), p(self.sin), p(kdst), 1)
+            R.ref_apply_rope(POS, NQ, 1, p(self.cos), p(self.sin), p(self.q), 0)
+            R.ref_o_proj(1, p(self.q), p(w["wo"]), p(self.attn_out))
+            R.ref_ffn(1, p(self.x), p(self.ffn_out), p(w["wu"]), p(w["wd"]), p(w["wg"]), p(self.ws))
+        R.ref_lm_head(1, p(self.x), p(self.lm), p(self.logits))
+        R.ref_sample_token_amax(p(self.logits), p(self.tok))
+
+
+# -------------------------------------------------------------- CPU baseline
+def cpu_baseline(seed: int):
+    """The CPU golden of the same step (oracle/ie_oracle.py restatement of
+    the reference generator's fp32 math) on the host cores, on a bounded
+    sample: one decoder layer's projections and the lm_head, each timed
+    (best of 3) and scaled to a 32-layer token."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import ie_oracle as oracle
+    cores = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(seed)
+
+    def w(*shape):
+        return oracle.round_dt(rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02), "bf16")
+
+    x = oracle.round_dt(rng.standard_normal((1, H), dtype=np.float32), "bf16")
+    layer = {"wq": w(NQ * HD, H), "wk": w(NKV * HD, H), "wv": w(NKV * HD, H), "wo": w(H, H), "wg": w(F, H),
+             "wu": w(F, H), "wd": w(H, F)}
+    cos, sin = oracle.rope_tables(CTX)
+
+    def one_layer():
+        q, k, v = oracle.qkv_cpu(x, layer["wq"], layer["wk"], layer["wv"], "bf16", POS, cos, sin)
+        oracle.gemm_cpu(q.transpose(1, 0, 2).reshape(1, H), layer["wo"], "bf16")
+        oracle.ffn_cpu(x, layer["wg"], layer["wu"], layer["wd"], "bf16")
+
+    def best(fn, n=3):
+        ts = []
+        for _ in range(n):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return min(ts)
+
+    t_layer = best(one_layer)
+    del layer
+    lm = w(V, H)
+    t_lm = best(lambda: oracle.lm_head_argmax_cpu(x, lm, "bf16"))
+    t_tok = L * t_layer + t_lm
+    return {"value": round(1.0 / t_tok, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"1 decoder layer (QKV+RoPE, O, FFN) best of 3 = {t_layer * 1e3:.1f} ms and lm_head+argmax "
+                      f"best of 3 = {t_lm * 1e3:.1f} ms, fp32 numpy BLAS on bf16-valued weights, scaled to "
+                      f"{L} layers + lm_head per token"}
+
+
+# ------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+
+    if args.impl == "reference" and rank != 0:
+        dist.destroy_process_group() if world > 1 else None
+        return
+
+    def barrier():
+        if world > 1 and args.impl == "ours":
+            dist.barrier()
+
+    hbm_peak, tf_peak, peak_src = load_peaks()
+    stream = torch.cuda.Stream(device=dev)
+    step = (OursStep if args.impl == "ours" else RefStep)(torch, dev, args.seed)
+    torch.cuda.synchronize()
+
+    graph = None
+    if args.impl == "ours":
+        with torch.cuda.stream(stream):
+            step()  # eager warm-up on the capture stream
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        run = graph.replay
+    else:
+        run = step
+        stream = torch.cuda.default_stream(dev)  # legacy default stream (the reference's)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            run()
+    torch.cuda.synchronize()
+
+    # ---------------- timed region (device events, max over ranks)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(args.steps):
+            run()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms_total = ev0.elapsed_time(ev1)
+    if world > 1 and args.impl == "ours":
+        t = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    tok_s = world * args.steps / (ms_total / 1e3) if args.impl == "ours" else args.steps / (ms_total / 1e3)
+
+    # ---------------- e2e: pinned H2D of the step input, replay, D2H token, per step
+    x_host = torch.empty_like(step.x, device="cpu").pin_memory()
+    x_host.copy_(step.x.cpu())
+    tok_host = torch.empty(1, dtype=torch.int32).pin_memory()
+    e2e_steps = max(5, args.steps // 2)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for _ in range(e2e_steps):
+            step.x.copy_(x_host, non_blocking=True)
+            run()
+            tok_host.copy_(step.tok, non_blocking=True)
+            stream.synchronize()
+            _ = int(tok_host[0])
+    e2e_s = time.perf_counter() - t0
+    if world > 1 and args.impl == "ours":
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": round((world if args.impl == "ours" else 1) * e2e_steps / e2e_s, 3), "unit": "tok/s",
+           "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+           "d2h_bytes_per_step": tok_host.numel() * tok_host.element_size()}
+
+    result = {
+        "metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16" if args.impl == "ours" else "f16",
+        "data": "synthetic: random-init Llama-3.1-8B-shaped weights N(0,0.02) (seeded), N(0,1) hidden state",
+        "config": {
+            "workload": "bs=1 decode weight-matmul path of Llama-3.1-8B: 32 x [fused QKV+RoPE (KV cache row 2047), "
+                        "O, FFN gate/up+SwiGLU, FFN down] + lm_head+argmax",
+            "batch": 1, "hidden": H, "ffn": F, "vocab": V, "layers": L,
+            "weight_bytes_per_step": WEIGHT_BYTES,
+            "l2": "inputs larger than L2 (15.01 GB of weights streamed per step)",
+            "parallelism": "replicas" if world > 1 else "single",
+            "launch": "one CUDA graph per step" if args.impl == "ours" else "eager, legacy default stream",
+        },
+        "matmul_hbm_gbs": round(WEIGHT_BYTES / (ms_step / 1e3) / 1e9, 1),
+        "e2e": e2e,
+        "clocks": clk,
+    }
+
+    if args.impl == "ours":
+        result["gpu_launches"] = step.launches_per_step * args.steps
+        # dominant kernel (FFN gate/up + SwiGLU, 54% of the bytes): 32 launches over
+        # distinct layer weights per replay, timed with events on its stream
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2, stream=stream):
+            step.gate_up_only()
+        reps = 10
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                g2.replay()
+            ev0.record(stream)
+            for _ in range(reps):
+                g2.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+        per_launch_s = ev0.elapsed_time(ev1) / 1e3 / (reps * L)
+        achieved = GATE_UP_BYTES / per_launch_s / 1e9
+        traffic = load_traffic()
+        result["roofline"] = {
+            "kernel": "skinny_kernel<bf16,1,EPI_SWIGLU> (FFN gate/up + SwiGLU, M=1)",
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
+            "traffic": traffic, "algorithmic_bytes_per_launch": GATE_UP_BYTES,
+            "avg_launch_us": round(per_launch_s * 1e6, 2),
+        }
+        result["step_roofline_frac"] = round(WEIGHT_BYTES / (ms_step / 1e3) / 1e9 / hbm_peak, 4)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline(args.seed)
+    else:
+        result["impl"] = "reference"
+        result["reference_build"] = ("Aryan470/infengine kernels/{ffn,swiglu,lm_head,sampling,attn,rope}.cu "
+                                     "compiled unchanged for sm_100a (oracle/Makefile), cuBLAS 12.9")
+        if not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline(args.seed)
+
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    del graph
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,172 @@
+/*
+ * infengine_b200 — C-ABI of the B200 (sm_100a) weight-matmul hot path.
+ *
+ * Every entry point:
+ *   - takes plain device pointers, element counts and a cudaStream_t passed as
+ *     `void*` (NULL = the legacy default stream, which is what the reference
+ *     launches on);
+ *   - allocates nothing: scratch is a caller-owned `workspace` sized by the
+ *     matching *_workspace_size() function;
+ *   - returns IE_OK (0) or a negative IE_ERR_* status; no C++ exception crosses
+ *     this boundary;
+ *   - validates shapes, pointer alignment (16 bytes for every matrix, leading
+ *     dimensions a multiple of 8 elements) before launching anything.
+ *
+ * Layouts follow the reference: row-major, weights are HF nn.Linear [out, in]
+ * ("W[N,K]"), and a projection computes Y[M,N] = X[M,K] . W[N,K]^T with fp32
+ * accumulation and one rounding to the storage type at the end.
+ *
+ * The reference interface each function replaces is cited as
+ * path:line inside the Aryan470/infengine tree.
+ */
+#ifndef INFENGINE_B200_H
+#define INFENGINE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define IE_OK                 0
+#define IE_ERR_INVALID_ARG   -1 /* null pointer, non-positive or inconsistent size */
+#define IE_ERR_ALIGNMENT     -2 /* pointer not 16-byte aligned or ld % 8 != 0     */
+#define IE_ERR_UNSUPPORTED   -3 /* shape / dtype combination has no kernel         */
+#define IE_ERR_LAUNCH        -4 /* CUDA reported an error at launch                 */
+#define IE_ERR_TIMEOUT       -5 /* a bounded device-side wait gave up               */
+#define IE_ERR_NO_DEVICE     -6 /* no CUDA device / not an sm_100 device            */
+#define IE_ERR_WORKSPACE     -7 /* workspace pointer null or smaller than required  */
+
+/* ---- element types ---------------------------------------------------- */
+typedef enum ie_dtype {
+  IE_DTYPE_F16 = 0,  /* the reference's storage type (kernels/*.cuh take half*)  */
+  IE_DTYPE_BF16 = 1  /* the BASELINE configs' storage type                        */
+} ie_dtype;
+
+/* Human-readable text of a status code (static storage). */
+const char* ie_status_string(int status);
+
+/* Library version, "major.minor.patch". */
+const char* ie_version(void);
+
+/* ---- a1 / a5: projection GEMM --------------------------------------------
+ * Replaces multiply_by_weight (kernels/ffn.cu:7-33, declared in
+ * kernels/multiply_by_weight.cuh:3) and the O projection
+ * multiply_preproj_Wo (kernels/attn.cu:265-293).
+ *   Y[M,N] = X[M,K] . W[N,K]^T ; X row stride ldx, W row stride ldw, Y row stride ldy.
+ * M <= 16 runs the decode kernel (weights streamed once with 128-bit loads and
+ * warp-level tensor-core dot products); larger M runs the tcgen05/TMEM GEMM.
+ */
+int ie_gemm(ie_dtype dt, int M, int N, int K,
+            const void* X, int64_t ldx,
+            const void* W, int64_t ldw,
+            void* Y, int64_t ldy,
+            void* stream);
+
+/* ---- a3: SwiGLU ------------------------------------------------------------
+ * Replaces swiglu (kernels/swiglu.cu:8-31, kernels/swiglu.cuh:5):
+ *   out[i] = g * (1 / (1 + expf(-g))) * u in fp32, rounded to dt.
+ * gate/up/out are [M, F] contiguous; out may alias gate or up.
+ */
+int ie_swiglu(ie_dtype dt, int M, int F,
+              const void* gate, const void* up, void* out, void* stream);
+
+/* ---- a2: FFN block -----------------------------------------------------------
+ * Replaces ffn / ffn_workspace_size (kernels/ffn.cu:35-64, kernels/ffn.cuh:5-6):
+ *   out = W_down . (silu(W_gate . x) * (W_up . x)).
+ * Argument order of the weights mirrors ffn(): up, down, gate.
+ * Gate and up are rounded to dt before SwiGLU and the SwiGLU product is
+ * rounded to dt before the down projection, as in the reference, but the
+ * gate/up pair is computed by one kernel whose epilogue applies SwiGLU, so
+ * only h[M,F] (not G and U) is written.
+ * x: [M,H], W_gate/W_up: [F,H], W_down: [H,F], out: [M,H].
+ */
+size_t ie_ffn_workspace_size(int M, int F);
+int ie_ffn(ie_dtype dt, int M, int H, int F,
+           const void* x, const void* W_up, const void* W_down, const void* W_gate,
+           void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* First half of ie_ffn on its own: h[M,F] (row stride ldh) =
+ * round(silu(round(x.W_gate^T)) * round(x.W_up^T)) — the gate/up GEMMs of
+ * kernels/ffn.cu:53-54 with swiglu (kernels/swiglu.cu:8-31) as their
+ * epilogue. With F a column shard of the FFN width this is the
+ * tensor-parallel gate/up step; the down projection of the shard is ie_gemm. */
+int ie_ffn_gate_up(ie_dtype dt, int M, int H, int F,
+                   const void* x, const void* W_gate, const void* W_up,
+                   void* h, int64_t ldh, void* stream);
+
+/* ---- a4: fused Q/K/V projection ------------------------------------------
+ * Replaces the three multiply_kqv_proj calls (kernels/attn.cu:12-39, called at
+ * :345-347 and :413-415) and, when rope_cos/rope_sin are non-NULL, the two
+ * apply_rope calls that follow them (kernels/rope.cu:20-66).
+ * One launch computes all n_q_heads + 2*n_kv_heads heads of x[M,H] and writes
+ * them head-major like the reference:
+ *   q_out  [n_q_heads][M][head_dim]                      (row m at token m)
+ *   k_cache[n_kv_heads][.][head_dim], row (pos0 + m), head stride cache_head_stride elements
+ *   v_cache same layout as k_cache.
+ * Wq: [n_q_heads*head_dim, H], Wk/Wv: [n_kv_heads*head_dim, H].
+ * RoPE (rotate-half, pairs (d, d+head_dim/2), table rows = position,
+ * table [*, head_dim/2] fp32) is applied to Q and K at position pos0 + m.
+ * head_dim must be 128 (the Llama-3.1 value, config.h:16).
+ */
+int ie_qkv(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_dim,
+           const void* x, const void* Wq, const void* Wk, const void* Wv,
+           void* q_out, void* k_cache, void* v_cache,
+           int64_t cache_head_stride, int pos0,
+           const float* rope_cos, const float* rope_sin,
+           void* stream);
+
+/* ---- a6 + a7: lm_head with fused greedy argmax --------------------------
+ * Replaces lm_head (kernels/lm_head.cu:5-20) followed by sample_token_amax
+ * (kernels/sampling.cu:54-58), for M rows at once.
+ * Computes logits[m, v] = round_dt(x[m,:] . W[v,:]) for the V rows of W (a
+ * vocab shard starting at global id vocab_offset) and picks per row m the
+ * index the reference's argmax would pick: the largest rounded logit; among
+ * equal logits the id whose (id mod 1024), bit-reversed over 10 bits, is
+ * smallest, then the smallest id (the order produced by amax_kern's strided
+ * scan over 1024 threads and reduce_amax's halving tree,
+ * kernels/sampling.cu:8-51).
+ * Outputs (each may be NULL): logits [M, ld_logits], idx_out [M] (global id),
+ * key_out [M] packed 64-bit keys; the max of keys across vocab shards is the
+ * key of the global winner (ie_argmax_key_index() recovers the id).
+ * workspace: ie_lm_head_argmax_workspace_size(M) bytes, zeroed once by the
+ * caller when allocated; every call leaves it zeroed again.
+ */
+size_t ie_lm_head_argmax_workspace_size(int M);
+int ie_lm_head_argmax(ie_dtype dt, int M, int K, int V, int64_t vocab_offset,
+                      const void* x, int64_t ldx, const void* W,
+                      void* logits, int64_t ld_logits,
+                      int* idx_out, unsigned long long* key_out,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- a7: argmax over stored logits ----------------------------------------
+ * Replaces sample_token_amax (kernels/sampling.cu:54-58, sampling.cuh:4) for
+ * M rows of V logits (row stride ld). Same tie rule as above. Needs no
+ * workspace: one thread-block cluster reduces each row through distributed
+ * shared memory.
+ */
+int ie_argmax(ie_dtype dt, int M, int V, const void* logits, int64_t ld,
+              int* idx_out, void* stream);
+
+/* Global vocabulary id held in a packed argmax key. */
+static inline int ie_argmax_key_index(unsigned long long key) {
+  unsigned int tie = ~(unsigned int)(key & 0xffffffffull);
+  unsigned int rr = tie >> 21, q = tie & ((1u << 21) - 1u), r = 0u, b;
+  for (b = 0; b < 10u; ++b) r |= ((rr >> b) & 1u) << (9u - b); /* undo the 10-bit reversal */
+  return (int)(q * 1024u + r);
+}
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* INFENGINE_B200_H */

@@ -1,0 +1,49 @@
+// Parameters of the prefill-path (M > 16) tcgen05/TMEM GEMM; see gemm_tc.cu.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "../../include/infengine_b200.h"
+
+namespace ie {
+
+enum TcEpilogue {
+  TC_EPI_STORE = 0,   // D[m, n] = round(acc)
+  TC_EPI_SWIGLU = 1,  // B = gate, B2 = up: D = round(silu(round(g)) * round(u))
+  TC_EPI_ARGMAX = 2,  // logits (optional) + per-row packed-key argmax
+  TC_EPI_QKV = 3,     // B/B2/B3 = Wq/Wk/Wv, head-major scatter + optional RoPE
+};
+
+// D[M, N] = A[M, K] . B[N, K]^T (A = activations, B = weights, both K-major).
+struct TcGemmParams {
+  const void* A = nullptr;
+  int64_t lda = 0;
+  const void* B = nullptr;
+  const void* B2 = nullptr;
+  const void* B3 = nullptr;
+  int64_t ldb = 0;
+  int M = 0, N = 0, K = 0;
+  void* D = nullptr;
+  int64_t ldd = 0;
+  int epi = TC_EPI_STORE;
+  // TC_EPI_ARGMAX
+  int64_t vocab_offset = 0;
+  unsigned long long* keys = nullptr;
+  unsigned int* counter = nullptr;
+  int* idx_out = nullptr;
+  unsigned long long* key_out = nullptr;
+  // TC_EPI_QKV
+  int n_q_heads = 0, n_kv_heads = 0;
+  void* q_out = nullptr;
+  int64_t q_head_stride = 0;
+  void* k_cache = nullptr;
+  void* v_cache = nullptr;
+  int64_t cache_head_stride = 0;
+  int pos0 = 0;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+};
+
+// Returns an IE_* status.
+int launch_tc_gemm(ie_dtype dt, const TcGemmParams& p, cudaStream_t st);
+
+}  // namespace ie

@@ -1,0 +1,48 @@
+// Parameters of the decode-path (M <= 16) kernels; see skinny.cu.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "../../include/infengine_b200.h"
+
+namespace ie {
+
+enum SkinnyEpilogue {
+  EPI_STORE = 0,   // Y[m, n] = round(acc)
+  EPI_SWIGLU = 1,  // two matrices (gate = W0, up = W1): Y = round(silu(round(g)) * round(u))
+  EPI_ARGMAX = 2,  // logits (optional store) + packed-key argmax per batch row
+  EPI_QKV = 3,     // head-major scatter of Q / K-cache / V-cache rows, optional RoPE
+};
+
+struct SkinnyParams {
+  const void* X = nullptr;
+  int64_t ldx = 0;
+  int M = 0, N = 0, K = 0;
+  const void* W0 = nullptr;
+  const void* W1 = nullptr;
+  const void* W2 = nullptr;
+  int64_t ldw = 0;
+  void* Y = nullptr;
+  int64_t ldy = 0;
+  // EPI_ARGMAX
+  int64_t vocab_offset = 0;
+  unsigned long long* keys = nullptr;
+  unsigned int* counter = nullptr;
+  int* idx_out = nullptr;
+  unsigned long long* key_out = nullptr;
+  // EPI_QKV
+  int n_q_heads = 0, n_kv_heads = 0;
+  void* q_out = nullptr;
+  int64_t q_head_stride = 0;
+  void* k_cache = nullptr;
+  void* v_cache = nullptr;
+  int64_t cache_head_stride = 0;
+  int pos0 = 0;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+};
+
+cudaError_t launch_skinny(ie_dtype dt, int epi, const SkinnyParams& p, cudaStream_t st);
+cudaError_t launch_swiglu(ie_dtype dt, int64_t n, const void* gate, const void* up, void* out, cudaStream_t st);
+cudaError_t launch_argmax(ie_dtype dt, int M, int V, const void* logits, int64_t ld, int* idx_out, cudaStream_t st);
+
+}  // namespace ie

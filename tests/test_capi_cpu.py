@@ -1,0 +1,107 @@
+"""CPU: the C-ABI library loads, exports what include/infengine_b200.h
+declares, and rejects bad arguments before touching a device."""
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "infengine_b200.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b(ie_\w+)\s*\(", text, flags=re.M)
+    static_inline = set(re.findall(r"static inline [\w\s\*]+?\b(ie_\w+)\s*\(", text))
+    return sorted(set(names) - static_inline)
+
+
+def test_header_declares_expected_entry_points():
+    names = declared_functions()
+    for n in ("ie_gemm", "ie_ffn", "ie_qkv", "ie_lm_head_argmax", "ie_argmax", "ie_swiglu"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(ie):
+    lib = ie.lib()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(ie.LIB_PATH)], capture_output=True, text=True).stdout
+    exported = {l.split()[-1] for l in out.splitlines() if " T " in l}
+    assert set(declared_functions()) <= exported
+    assert set(ie.EXPORTED_SYMBOLS) <= exported
+
+
+def test_dropin_library_exports_reference_signatures(ie):
+    out = subprocess.run(["nm", "-DC", "--defined-only", str(ie.DROPIN_PATH)], capture_output=True,
+                         text=True).stdout
+    for sig in (
+        "multiply_by_weight(cublasContext*, int, int, int, __half const*, __half const*, __half*)",
+        "ffn(cublasContext*, int, __half*, __half*, __half*, __half*, __half*, void*)",
+        "ffn_workspace_size(int)",
+        "swiglu(int, __half*, __half*, __half*)",
+        "lm_head(cublasContext*, int, __half*, __half*, __half*)",
+        "sample_token_amax(__half const*, int*)",
+    ):
+        assert sig in out, sig
+
+
+def test_status_strings(ie):
+    lib = ie.lib()
+    assert lib.ie_status_string(0) == b"ok"
+    for code, text in ie.STATUS.items():
+        assert lib.ie_status_string(code).decode() == text
+    assert lib.ie_version().decode().count(".") == 2
+
+
+def test_invalid_arguments_rejected_without_device(ie):
+    lib = ie.lib()
+    vp = ctypes.c_void_p
+    fake = vp(0x1000)  # never dereferenced: validation fails first
+    # bad dtype
+    assert lib.ie_gemm(7, 1, 16, 16, fake, 16, fake, 16, fake, 16, None) == -1
+    # null operands
+    assert lib.ie_gemm(1, 1, 16, 16, None, 16, fake, 16, fake, 16, None) == -1
+    # K not a multiple of 8
+    assert lib.ie_gemm(1, 1, 16, 12, fake, 12, fake, 12, fake, 16, None) == -2
+    # misaligned pointer
+    assert lib.ie_gemm(1, 1, 16, 16, vp(0x1002), 16, fake, 16, fake, 16, None) == -2
+    # leading dimension smaller than K
+    assert lib.ie_gemm(1, 1, 16, 16, fake, 8, fake, 16, fake, 16, None) == -1
+    # empty problems are a no-op
+    assert lib.ie_gemm(1, 0, 16, 16, fake, 16, fake, 16, fake, 16, None) == 0
+    # head_dim other than 128
+    assert lib.ie_qkv(1, 1, 4096, 32, 8, 64, fake, fake, fake, fake, fake, fake, fake, 8192 * 64, 0,
+                      None, None, None) == -3
+    # ffn workspace too small
+    assert lib.ie_ffn(1, 1, 4096, 14336, fake, fake, fake, fake, fake, fake, 16, None) == -7
+    # lm_head workspace missing
+    assert lib.ie_lm_head_argmax(1, 1, 4096, 128256, 0, fake, 4096, fake, None, 0, None, None, None, 0,
+                                 None) == -7
+    # vocab ids must fit the packed key (id < 2^31)
+    assert lib.ie_lm_head_argmax(1, 1, 4096, 16, 2 ** 31, fake, 4096, fake, None, 0, None, None, fake, 4096,
+                                 None) == -3
+    # argmax leading dimension smaller than V
+    assert lib.ie_argmax(0, 1, 100, fake, 50, fake, None) == -1
+
+
+def test_workspace_sizes(ie):
+    assert ie.ffn_workspace_bytes(1, 14336) >= 14336 * 2
+    assert ie.ffn_workspace_size(5) == 2 * 5 * 14336 * 2  # reference ffn.cu:35-37
+    assert ie.lm_head_workspace_bytes(64) >= 64 * 8 + 4
+
+
+def test_key_index_roundtrip(ie):
+    from conftest import oracle
+    for idx in (0, 1, 1023, 1024, 75177, 128255, 2 ** 31 - 1):
+        assert ie.key_index(oracle.argmax_key(1.5, idx)) == idx
+
+
+def test_python_mirror_fails_loudly_without_library(monkeypatch, ie, tmp_path):
+    monkeypatch.setattr(ie, "LIB_PATH", tmp_path / "missing.so")
+    monkeypatch.setattr(ie, "_lib_handle", None)
+    with pytest.raises(RuntimeError, match="missing"):
+        ie.lib()

@@ -1,0 +1,131 @@
+"""GPU parity against the reference's own code (oracle/_ref, built from the
+reference's kernels/*.cu for sm_100a, cuBLAS 12.9 underneath), on identical
+fp16 inputs. Also pins the oracle's argmax restatement against the
+reference's amax_kern on crafted tie vectors."""
+import numpy as np
+import pytest
+
+from conftest import from_dev, oracle, to_dev, ulp
+from ref_lib import p, ref
+
+pytestmark = pytest.mark.gpu
+
+
+def test_reference_argmax_pins_oracle_tie_rule(ie, cuda):
+    R = ref()
+    rng = np.random.default_rng(1)
+    cases = []
+    v = np.zeros(128256, np.float32)
+    v[3074] = v[512] = 1.0
+    cases.append(v)
+    v = np.zeros(128256, np.float32)
+    v[5] = v[1024] = 3.0
+    cases.append(v)
+    for _ in range(6):
+        cases.append(oracle.round_dt(rng.integers(-3, 4, size=128256) * 0.5, "f16"))
+    out_ref = cuda.zeros((1,), dtype=cuda.int32, device="cuda")
+    out_ie = cuda.zeros((1,), dtype=cuda.int32, device="cuda")
+    for v in cases:
+        t = to_dev(v, "f16")
+        R.ref_sample_token_amax(p(t), p(out_ref))
+        ie.sample_token_amax(t, out_ie)
+        cuda.cuda.synchronize()
+        want = int(out_ref.item())
+        assert oracle.argmax_reference(v) == want
+        assert int(out_ie.item()) == want
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 4096, 4096), (1, 4096, 14336), (4, 14336, 4096), (8, 4096, 6144)])
+def test_multiply_by_weight_vs_reference(ie, cuda, m, k, n):
+    R = ref()
+    d = oracle.seeded_inputs(m + n, {"x": (m, k), "w": (n, k)}, "f16")
+    x, w = to_dev(d["x"], "f16"), to_dev(d["w"], "f16")
+    y_ref = cuda.empty((m, n), dtype=cuda.float16, device="cuda")
+    y_ie = cuda.empty((m, n), dtype=cuda.float16, device="cuda")
+    R.ref_multiply_by_weight(m, k, n, p(x), p(w), p(y_ref))
+    ie.multiply_by_weight(m, k, n, x, w, y_ie)
+    cuda.cuda.synchronize()
+    a, b = from_dev(y_ie), from_dev(y_ref)
+    # both round an fp32 accumulation: at most one rounding step apart
+    assert np.all(np.abs(a - b) <= ulp(np.maximum(np.abs(a), np.abs(b)), "f16") * 1.01 + 1e-6)
+    assert np.mean(a == b) > 0.9
+
+
+@pytest.mark.parametrize("M", [1, 4, 8])
+def test_ffn_vs_reference(ie, cuda, M):
+    R = ref()
+    H, F = 4096, 14336
+    d = oracle.seeded_inputs(300 + M, {"x": (M, H), "wg": (F, H), "wu": (F, H), "wd": (H, F)}, "f16")
+    x = to_dev(d["x"], "f16")
+    wu, wd, wg = to_dev(d["wu"], "f16"), to_dev(d["wd"], "f16"), to_dev(d["wg"], "f16")
+    ws_ref = cuda.empty(R.ref_ffn_workspace_size(M), dtype=cuda.uint8, device="cuda")
+    ws_ie = cuda.empty(ie.ffn_workspace_size(M), dtype=cuda.uint8, device="cuda")
+    o_ref = cuda.empty((M, H), dtype=cuda.float16, device="cuda")
+    o_ie = cuda.empty((M, H), dtype=cuda.float16, device="cuda")
+    R.ref_ffn(M, p(x), p(o_ref), p(wu), p(wd), p(wg), p(ws_ref))
+    ie.ffn(M, x, o_ie, wu, wd, wg, ws_ie)
+    cuda.cuda.synchronize()
+    a, b = from_dev(o_ie), from_dev(o_ref)
+    # reference test_ffn.cu:39-42 uses atol 1e-3 on outputs of scale ~0.05;
+    # these random-init outputs have scale ~2.5, so the bound is relative
+    assert oracle.normwise_rel_err(a, b) <= 2e-3
+    r = oracle.compare(a, b, atol=2 * 2.0 ** -10 * np.abs(b).max())
+    assert r["pct_within_tol"] > 99.0
+
+
+def test_lm_head_and_sampling_vs_reference(ie, cuda):
+    """lm_head (last row of a 3-token input) + sample_token_amax, fp16."""
+    R = ref()
+    S, K, V = 3, 4096, 128256
+    for seed in range(3):
+        d = oracle.seeded_inputs(500 + seed, {"x": (S, K), "w": (V, K)}, "f16")
+        x, w = to_dev(d["x"], "f16"), to_dev(d["w"], "f16")
+        l_ref = cuda.empty((V,), dtype=cuda.float16, device="cuda")
+        l_ie = cuda.empty((V,), dtype=cuda.float16, device="cuda")
+        t_ref = cuda.zeros((1,), dtype=cuda.int32, device="cuda")
+        t_ie = cuda.zeros((1,), dtype=cuda.int32, device="cuda")
+        R.ref_lm_head(S, p(x), p(w), p(l_ref))
+        R.ref_sample_token_amax(p(l_ref), p(t_ref))
+        ie.lm_head(S, x, w, l_ie)
+        ie.sample_token_amax(l_ie, t_ie)
+        # fused path on the same input row
+        ws = cuda.zeros(ie.lm_head_workspace_bytes(1), dtype=cuda.uint8, device="cuda")
+        t_fused = cuda.zeros((1,), dtype=cuda.int32, device="cuda")
+        ie.lm_head_argmax(x[S - 1:S], w, ws, idx_out=t_fused)
+        cuda.cuda.synchronize()
+        a, b = from_dev(l_ie), from_dev(l_ref)
+        assert np.all(np.abs(a - b) <= ulp(np.maximum(np.abs(a), np.abs(b)), "f16") * 1.01 + 1e-6)
+        assert int(t_fused.item()) == int(t_ie.item())
+        # same sampler on the reference's logits gives the reference's token
+        ie.sample_token_amax(l_ref, t_ie)
+        cuda.cuda.synchronize()
+        assert int(t_ie.item()) == int(t_ref.item())
+
+
+@pytest.mark.parametrize("M,pos0", [(1, 2047), (4, 0)])
+def test_qkv_rope_vs_reference(ie, cuda, M, pos0):
+    """Fused QKV+RoPE vs the reference's three strided-batched GEMMs + two
+    apply_rope launches (kernels/attn.cu:411-420)."""
+    R = ref()
+    H, nq, nkv, hd, ctx = 4096, 32, 8, 128, 8192
+    d = oracle.seeded_inputs(900 + M, {"x": (M, H), "wq": (nq * hd, H), "wk": (nkv * hd, H),
+                                       "wv": (nkv * hd, H)}, "f16")
+    cos, sin = oracle.rope_tables(ctx)
+    c_t, s_t = cuda.from_numpy(cos).cuda(), cuda.from_numpy(sin).cuda()
+    x = to_dev(d["x"], "f16")
+    wq, wk, wv = (to_dev(d[k], "f16") for k in ("wq", "wk", "wv"))
+    q_r = cuda.zeros((nq, M, hd), dtype=cuda.float16, device="cuda")
+    k_r = cuda.zeros((nkv, ctx, hd), dtype=cuda.float16, device="cuda")
+    v_r = cuda.zeros((nkv, ctx, hd), dtype=cuda.float16, device="cuda")
+    R.ref_qkv_proj(M, p(x), p(wq), p(wk), p(wv), p(q_r), p(k_r[:, pos0]), p(v_r[:, pos0]), nq, nkv)
+    R.ref_apply_rope(pos0, nkv, M, p(c_t), p(s_t), p(k_r[:, pos0]), 1)
+    R.ref_apply_rope(pos0, nq, M, p(c_t), p(s_t), p(q_r), 0)
+    q_i = cuda.zeros_like(q_r)
+    k_i = cuda.zeros_like(k_r)
+    v_i = cuda.zeros_like(v_r)
+    ie.qkv(x, wq, wk, wv, q_i, k_i, v_i, ctx * hd, pos0, c_t, s_t)
+    cuda.cuda.synchronize()
+    for a_t, b_t in ((q_i, q_r), (k_i, k_r), (v_i, v_r)):
+        a, b = from_dev(a_t), from_dev(b_t)
+        tol = 2 * ulp(np.maximum(np.abs(a), np.abs(b)), "f16") + 1e-3 * np.abs(b).max()
+        assert np.all(np.abs(a - b) <= tol)
