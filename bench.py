@@ -20,8 +20,11 @@ for the same path, compiled from its sources for sm_100a (cuBLAS GEMMs,
 its RoPE, SwiGLU and argmax kernels; fp16, the reference's only dtype),
 launched eagerly on the legacy default stream as its decode loop does.
 
-For N > 1 (torchrun) every rank runs a full replica (weak scaling); the
-printed value is the sum over ranks, timed as the max over ranks.
+For N > 1 (torchrun) the same token stream is split by tensor parallelism
+(infengine_b200.tp: Q/K/V and gate/up column-split, O and down row-split with
+an fp32 NCCL allreduce, lm_head vocabulary-split with a max over packed argmax
+keys); the value is tok/s of the one stream (strong scaling), timed as the
+max over ranks.
 """
 from __future__ import annotations
 
@@ -49,11 +52,13 @@ GATE_UP_BYTES = 2 * (2 * F * H + H + F)  # one gate/up+SwiGLU launch at M=1
 
 
 def load_peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, bf16 TFLOP/s sustained, source)."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
-    return 6650.0, 1590.0, "fallback"
+        return (float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "measured")
+    return 6650.0, 1590.0, 1400.0, "fallback"
 
 
 def load_traffic():
@@ -176,6 +181,82 @@ class OursStep:
         for w in self.layers:
             self.ie.ffn_gate_up(self.x, w["wg"], w["wu"], self.h)
 
+    def setup_prefill(self, S: int):
+        """Buffers for the M=S prefill projection chain over the same weights."""
+        torch, dev = self.torch, self.x.device
+        g = torch.Generator(device=dev)
+        g.manual_seed(7)
+        self.S = S
+        self.xp = torch.randn(S, H, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+        self.qp = torch.empty(NQ, S, HD, device=dev, dtype=torch.bfloat16)
+        self.ap = torch.empty(S, H, device=dev, dtype=torch.bfloat16)
+        self.hp = torch.empty(S, F, device=dev, dtype=torch.bfloat16)
+        self.op = torch.empty(S, H, device=dev, dtype=torch.bfloat16)
+
+    def prefill(self):
+        """32 x [fused QKV+RoPE, O, gate/up+SwiGLU, down] at M = S tokens (positions 0..S-1)."""
+        ie, S = self.ie, self.S
+        for l, w in enumerate(self.layers):
+            ie.qkv(self.xp, w["wq"], w["wk"], w["wv"], self.qp, self.kc[l], self.vc[l], CTX * HD, 0, self.cos,
+                   self.sin)
+            ie.gemm(self.qp.view(S, H), w["wo"], self.ap)  # stand-in for the attention output
+            ie.ffn_gate_up(self.xp, w["wg"], w["wu"], self.hp)
+            ie.gemm(self.hp, w["wd"], self.op)
+
+    def prefill_flops(self):
+        return 2.0 * self.S * L * LAYER_WEIGHT_ELEMS
+
+
+# ------------------------------------------------------ our arm, N GPUs (TP)
+class TPStep:
+    """Tensor-parallel decode step (infengine_b200.tp): rank r holds 1/N of
+    every projection; O and down partial sums are allreduced in fp32 over
+    NCCL and the vocabulary-split lm_head is merged by a max over packed
+    argmax keys. Every rank draws the full seeded weights layer by layer and
+    keeps its shard, so the model is the one the single-GPU arm runs."""
+
+    def __init__(self, torch, dev, seed, world, rank):
+        import infengine_b200 as ie
+        from infengine_b200.host import rope_tables
+        from infengine_b200.tp import Comm, ShardPlan, TPDecodeStep
+        self.ie, self.torch = ie, torch
+        self.plan = ShardPlan(world, rank)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+
+        def w(*shape):
+            return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32).mul_(0.02).to(torch.bfloat16)
+
+        layers = []
+        for _ in range(L):
+            full = {"wq": w(NQ * HD, H), "wk": w(NKV * HD, H), "wv": w(NKV * HD, H), "wo": w(H, H),
+                    "wg": w(F, H), "wu": w(F, H), "wd": w(H, F)}
+            layers.append(self.plan.shard_layer(full))
+            del full
+        lm = self.plan.shard_lm_head(w(V, H))
+        torch.cuda.empty_cache()
+        cos, sin = rope_tables(CTX)
+        self.comm = Comm(world, rank)
+        self.inner = TPDecodeStep(self.plan, self.comm, layers, lm, torch.from_numpy(cos).to(dev),
+                                  torch.from_numpy(sin).to(dev), POS)
+        g2 = torch.Generator(device=dev)
+        g2.manual_seed(seed + 1)
+        self.inner.x.copy_(torch.randn(1, H, generator=g2, device=dev, dtype=torch.float32).to(torch.bfloat16))
+        self.x, self.tok = self.inner.x, self.inner.tok
+        self.launches_per_step = self.inner.launches_per_step
+        self.layers = layers
+        self.h = self.inner.h
+
+    def __call__(self):
+        self.inner()
+
+    def gate_up_only(self):
+        for w in self.layers:
+            self.ie.ffn_gate_up(self.x, w["wg"], w["wu"], self.h)
+
+    def close(self):
+        self.comm.close()
+
 
 # ---------------------------------------------------------- reference arm
 class RefStep:
@@ -259,6 +340,71 @@ def cpu_baseline(seed: int):
                       f"{L} layers + lm_head per token"}
 
 
+# --------------------------------------------------------- single-kernel cases
+def single_case(torch, name: str, steps: int, seed: int):
+    """A few launches of one hot-path kernel on one layer's weights (a small
+    workload for ncu captures; inputs still exceed the L2)."""
+    import infengine_b200 as ie
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    bf = torch.bfloat16
+
+    def w(*shape):
+        return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32).mul_(0.02).to(bf)
+
+    x = torch.randn(1, H, generator=g, device=dev, dtype=torch.float32).to(bf)
+    if name == "gate_up":
+        wg, wu, h = w(F, H), w(F, H), torch.empty(1, F, device=dev, dtype=bf)
+        fn = lambda: ie.ffn_gate_up(x, wg, wu, h)
+    elif name == "down":
+        wd, hh, out = w(H, F), torch.randn(1, F, device=dev).to(bf), torch.empty(1, H, device=dev, dtype=bf)
+        fn = lambda: ie.gemm(hh, wd, out)
+    elif name == "o":
+        wo, out = w(H, H), torch.empty(1, H, device=dev, dtype=bf)
+        fn = lambda: ie.gemm(x, wo, out)
+    elif name == "qkv":
+        from infengine_b200.host import rope_tables
+        wq, wk, wv = w(NQ * HD, H), w(NKV * HD, H), w(NKV * HD, H)
+        q = torch.empty(NQ, 1, HD, device=dev, dtype=bf)
+        kc, vc = torch.zeros(NKV, CTX, HD, device=dev, dtype=bf), torch.zeros(NKV, CTX, HD, device=dev, dtype=bf)
+        cos, sin = (torch.from_numpy(t).to(dev) for t in rope_tables(CTX))
+        fn = lambda: ie.qkv(x, wq, wk, wv, q, kc, vc, CTX * HD, POS, cos, sin)
+    elif name == "lm_head":
+        lm = w(V, H)
+        ws = torch.zeros(ie.lm_head_workspace_bytes(1), dtype=torch.uint8, device=dev)
+        tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        fn = lambda: ie.lm_head_argmax(x, lm, ws, idx_out=tok)
+    elif name.startswith("prefill_"):
+        S = 2048
+        xs = torch.randn(S, H, generator=g, device=dev, dtype=torch.float32).to(bf)
+        kind = name[len("prefill_"):]
+        if kind == "o":
+            wo, out = w(H, H), torch.empty(S, H, device=dev, dtype=bf)
+            fn = lambda: ie.gemm(xs, wo, out)
+        elif kind == "down":
+            wd, hs, out = w(H, F), torch.randn(S, F, device=dev).to(bf), torch.empty(S, H, device=dev, dtype=bf)
+            fn = lambda: ie.gemm(hs, wd, out)
+        elif kind == "gate_up":
+            wg, wu, hs = w(F, H), w(F, H), torch.empty(S, F, device=dev, dtype=bf)
+            fn = lambda: ie.ffn_gate_up(xs, wg, wu, hs)
+        elif kind == "qkv":
+            from infengine_b200.host import rope_tables
+            wq, wk, wv = w(NQ * HD, H), w(NKV * HD, H), w(NKV * HD, H)
+            q = torch.empty(NQ, S, HD, device=dev, dtype=bf)
+            kc, vc = torch.zeros(NKV, CTX, HD, device=dev, dtype=bf), torch.zeros(NKV, CTX, HD, device=dev, dtype=bf)
+            cos, sin = (torch.from_numpy(t).to(dev) for t in rope_tables(CTX))
+            fn = lambda: ie.qkv(xs, wq, wk, wv, q, kc, vc, CTX * HD, 0, cos, sin)
+        else:
+            raise SystemExit(f"unknown case {name}")
+    else:
+        raise SystemExit(f"unknown case {name}")
+    for _ in range(steps):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"case": name, "launches": steps}))
+
+
 # ------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -268,12 +414,18 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", default=None,
+                    help="run only one kernel (gate_up|down|o|qkv|lm_head) --steps times, for profiling")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
 
     import torch
     import torch.distributed as dist
+
+    if args.case:
+        single_case(torch, args.case, args.steps, args.seed)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -293,9 +445,12 @@ def main():
         if world > 1 and args.impl == "ours":
             dist.barrier()
 
-    hbm_peak, tf_peak, peak_src = load_peaks()
+    hbm_peak, tf_peak, tf_peak_sus, peak_src = load_peaks()
     stream = torch.cuda.Stream(device=dev)
-    step = (OursStep if args.impl == "ours" else RefStep)(torch, dev, args.seed)
+    if args.impl == "ours" and world > 1:
+        step = TPStep(torch, dev, args.seed, world, rank)
+    else:
+        step = (OursStep if args.impl == "ours" else RefStep)(torch, dev, args.seed)
     torch.cuda.synchronize()
 
     graph = None
@@ -338,7 +493,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_total = float(t.item())
     ms_step = ms_total / args.steps
-    tok_s = world * args.steps / (ms_total / 1e3) if args.impl == "ours" else args.steps / (ms_total / 1e3)
+    tok_s = args.steps / (ms_total / 1e3)  # one token stream (tensor parallel at N > 1)
 
     # ---------------- e2e: pinned H2D of the step input, replay, D2H token, per step
     x_host = torch.empty_like(step.x, device="cpu").pin_memory()
@@ -360,13 +515,13 @@ def main():
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = {"value": round((world if args.impl == "ours" else 1) * e2e_steps / e2e_s, 3), "unit": "tok/s",
+    e2e = {"value": round(e2e_steps / e2e_s, 3), "unit": "tok/s",
            "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
            "d2h_bytes_per_step": tok_host.numel() * tok_host.element_size()}
 
     result = {
         "metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16" if args.impl == "ours" else "f16",
         "data": "synthetic: random-init Llama-3.1-8B-shaped weights N(0,0.02) (seeded), N(0,1) hidden state",
         "config": {
@@ -375,7 +530,7 @@ def main():
             "batch": 1, "hidden": H, "ffn": F, "vocab": V, "layers": L,
             "weight_bytes_per_step": WEIGHT_BYTES,
             "l2": "inputs larger than L2 (15.01 GB of weights streamed per step)",
-            "parallelism": "replicas" if world > 1 else "single",
+            "parallelism": f"tp{world}" if world > 1 else "single",
             "launch": "one CUDA graph per step" if args.impl == "ours" else "eager, legacy default stream",
         },
         "matmul_hbm_gbs": round(WEIGHT_BYTES / (ms_step / 1e3) / 1e9, 1),
@@ -400,19 +555,48 @@ def main():
             ev1.record(stream)
         torch.cuda.synchronize()
         per_launch_s = ev0.elapsed_time(ev1) / 1e3 / (reps * L)
-        achieved = GATE_UP_BYTES / per_launch_s / 1e9
+        f_local = step.h.shape[1]
+        gate_up_bytes = 2 * (2 * f_local * H + H + f_local)
+        achieved = gate_up_bytes / per_launch_s / 1e9
         traffic = load_traffic()
         result["roofline"] = {
-            "kernel": "skinny_kernel<bf16,1,EPI_SWIGLU> (FFN gate/up + SwiGLU, M=1)",
+            "kernel": f"skinny_kernel<bf16,1,EPI_SWIGLU> (FFN gate/up + SwiGLU, M=1, {f_local} rows)",
             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
-            "traffic": traffic, "algorithmic_bytes_per_launch": GATE_UP_BYTES,
+            "traffic": traffic if world == 1 else None, "algorithmic_bytes_per_launch": gate_up_bytes,
             "avg_launch_us": round(per_launch_s * 1e6, 2),
         }
-        result["step_roofline_frac"] = round(WEIGHT_BYTES / (ms_step / 1e3) / 1e9 / hbm_peak, 4)
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["step_roofline_frac"] = round(WEIGHT_BYTES / world / (ms_step / 1e3) / 1e9 / hbm_peak, 4)
+    if args.impl == "ours" and world == 1:
+        # prefill projection GEMMs at M=2048 over all 32 layers
+        step.setup_prefill(2048)
+        gp = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            step.prefill()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(gp, stream=stream):
+            step.prefill()
+        reps = 3
+        with torch.cuda.stream(stream):
+            gp.replay()
+            ev0.record(stream)
+            for _ in range(reps):
+                gp.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+        pre_s = ev0.elapsed_time(ev1) / 1e3 / reps
+        tflops = step.prefill_flops() / pre_s / 1e12
+        result["prefill"] = {
+            "workload": "M=2048 tokens: 32 x [fused QKV+RoPE 6144x4096, O 4096x4096, gate/up+SwiGLU 2x14336x4096, "
+                        "down 4096x14336]", "ms": round(pre_s * 1e3, 3), "tflops": round(tflops, 1),
+            "peak_tflops": tf_peak_sus, "frac": round(tflops / tf_peak_sus, 4),
+            "peak_source": f"{peak_src} bf16 sustained (a {pre_s * 1e3:.0f} ms chain)",
+            "gpu_launches": 4 * L,
+        }
+        del gp
+        if rank == 0 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(args.seed)
-    else:
+    elif args.impl == "reference":
         result["impl"] = "reference"
         result["reference_build"] = ("Aryan470/infengine kernels/{ffn,swiglu,lm_head,sampling,attn,rope}.cu "
                                      "compiled unchanged for sm_100a (oracle/Makefile), cuBLAS 12.9")
@@ -421,7 +605,9 @@ def main():
 
     if rank == 0:
         print(json.dumps(result), flush=True)
-    del graph
+    del graph  # graphs holding NCCL work go before the communicators
+    if hasattr(step, "close"):
+        step.close()
     if world > 1:
         dist.destroy_process_group()
 

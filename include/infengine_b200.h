@@ -55,6 +55,12 @@ const char* ie_status_string(int status);
 /* Library version, "major.minor.patch". */
 const char* ie_version(void);
 
+/* Device-side status of the current device: IE_OK, or IE_ERR_TIMEOUT when a
+ * bounded wait inside a tensor-core kernel gave up (the kernel then drained
+ * its own copies, freed its tensor memory and returned without finishing).
+ * Synchronizes the device. clear != 0 resets the word to IE_OK. */
+int ie_device_status(int clear);
+
 /* ---- a1 / a5: projection GEMM --------------------------------------------
  * Replaces multiply_by_weight (kernels/ffn.cu:7-33, declared in
  * kernels/multiply_by_weight.cuh:3) and the O projection
@@ -68,6 +74,15 @@ int ie_gemm(ie_dtype dt, int M, int N, int K,
             const void* W, int64_t ldw,
             void* Y, int64_t ldy,
             void* stream);
+
+/* Same projection with unrounded fp32 output Y[M,N] (row stride ldy floats,
+ * 16-byte aligned): the partial sums of a row-split (tensor-parallel) O or
+ * down projection, to be summed across ranks before the one rounding. */
+int ie_gemm_f32out(ie_dtype dt, int M, int N, int K,
+                   const void* X, int64_t ldx,
+                   const void* W, int64_t ldw,
+                   float* Y, int64_t ldy,
+                   void* stream);
 
 /* ---- a3: SwiGLU ------------------------------------------------------------
  * Replaces swiglu (kernels/swiglu.cu:8-31, kernels/swiglu.cuh:5):
@@ -153,6 +168,28 @@ int ie_lm_head_argmax(ie_dtype dt, int M, int K, int V, int64_t vocab_offset,
  */
 int ie_argmax(ie_dtype dt, int M, int V, const void* logits, int64_t ld,
               int* idx_out, void* stream);
+
+/* ---- e1: tensor-parallel exchange steps -------------------------------------
+ * No counterpart in the reference (single GPU only). Megatron-style split of
+ * the path: Q/K/V by heads and gate/up by FFN rows (ie_qkv / ie_ffn_gate_up
+ * on the shard), O and down by their input columns (ie_gemm_f32out on the
+ * shard, then ie_allreduce_sum_f32, then ie_cast_f32), lm_head by vocabulary
+ * rows (ie_lm_head_argmax with vocab_offset and key_out, then
+ * ie_argmax_allreduce). The exchanges use NCCL, loaded at run time from the
+ * process ("libnccl.so.2"); IE_ERR_UNSUPPORTED when it cannot be found.
+ * The communicator is created once per rank from a 128-byte unique id that
+ * rank 0 makes with ie_comm_unique_id and the caller distributes. */
+typedef struct ie_comm ie_comm;
+int ie_comm_unique_id(void* out_128_bytes);
+int ie_comm_create(int nranks, int rank, const void* unique_id, ie_comm** out);
+int ie_comm_destroy(ie_comm* comm);
+/* In-place sum over ranks of count floats. */
+int ie_allreduce_sum_f32(ie_comm* comm, float* buf, size_t count, void* stream);
+/* In-place max over ranks of M packed argmax keys; idx_out (nullable) [M]
+ * receives the winning global vocabulary ids. */
+int ie_argmax_allreduce(ie_comm* comm, unsigned long long* keys, int M, int* idx_out, void* stream);
+/* out[i] = round_dt(in[i]) for n values. */
+int ie_cast_f32(ie_dtype dt, const float* in, void* out, size_t n, void* stream);
 
 /* Global vocabulary id held in a packed argmax key. */
 static inline int ie_argmax_key_index(unsigned long long key) {

@@ -52,7 +52,7 @@ STATUS = {
 
 EXPORTED_SYMBOLS = (
     "ie_status_string", "ie_version", "ie_gemm", "ie_swiglu", "ie_ffn_workspace_size", "ie_ffn", "ie_ffn_gate_up",
-    "ie_qkv", "ie_lm_head_argmax_workspace_size", "ie_lm_head_argmax", "ie_argmax",
+    "ie_qkv", "ie_lm_head_argmax_workspace_size", "ie_lm_head_argmax", "ie_argmax", "ie_device_status",
 )
 
 
@@ -76,6 +76,8 @@ def lib() -> ctypes.CDLL:
         L.ie_status_string.restype = ctypes.c_char_p
         L.ie_status_string.argtypes = [i32]
         L.ie_version.restype = ctypes.c_char_p
+        L.ie_device_status.argtypes = [i32]
+        L.ie_device_status.restype = i32
         L.ie_gemm.argtypes = [i32, i32, i32, i32, vp, i64, vp, i64, vp, i64, vp]
         L.ie_swiglu.argtypes = [i32, i32, i32, vp, vp, vp, vp]
         L.ie_ffn_workspace_size.restype = sz
@@ -187,6 +189,11 @@ def argmax(logits, idx_out, stream=None):
     M, V = logits.shape
     _check(lib().ie_argmax(_dt(logits), M, V, _ptr(logits), logits.stride(0), _ptr(idx_out), _stream(stream)),
            "ie_argmax")
+
+
+def device_status(clear: bool = True) -> int:
+    """ie_device_status: IE_OK or IE_ERR_TIMEOUT from a bounded device wait."""
+    return int(lib().ie_device_status(1 if clear else 0))
 
 
 def key_index(key: int) -> int:

@@ -28,7 +28,7 @@ CFLAGS = ARCH + [
     "-I", str(ROOT / "include"), "--expt-relaxed-constexpr",
 ]
 
-CORE_SOURCES = ["capi.cu", "skinny.cu", "gemm_tc.cu"]
+CORE_SOURCES = ["capi.cu", "skinny.cu", "gemm_tc.cu", "comm.cu"]
 DROPIN_SOURCES = ["dropin.cu"]
 
 LIB_CORE = PKG / "libinfengine_b200.so"
@@ -70,7 +70,7 @@ def build(force: bool = False, verbose: bool = False) -> list[Path]:
         dropin_objs = list(ex.map(lambda s: _compile(s, force), DROPIN_SOURCES))
     if force or not _newer(LIB_CORE, core_objs):
         _run([NVCC, *ARCH, "-shared", "--cudart", "static", "-o", str(LIB_CORE), *map(str, core_objs),
-              "-Xlinker", "-Bsymbolic"])
+              "-ldl", "-Xlinker", "-Bsymbolic"])
     if force or not _newer(LIB_DROPIN, dropin_objs + [LIB_CORE]):
         _run([NVCC, *ARCH, "-shared", "-o", str(LIB_DROPIN), *map(str, dropin_objs),
               "-L", str(PKG), "-linfengine_b200", "-Xlinker", "-rpath,$ORIGIN", "--cudart", "static", "-ldl",

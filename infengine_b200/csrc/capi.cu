@@ -52,6 +52,11 @@ const char* ie_status_string(int status) {
 
 const char* ie_version(void) { return "0.1.0"; }
 
+int ie_device_status(int clear) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return IE_ERR_LAUNCH;
+  return read_tc_status(clear != 0);
+}
+
 int ie_gemm(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, void* Y,
             int64_t ldy, void* stream) {
   if (!valid_dtype(dt) || M < 0 || N < 0 || K <= 0) return IE_ERR_INVALID_ARG;
@@ -70,6 +75,27 @@ int ie_gemm(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const 
   TcGemmParams q;
   q.A = X; q.lda = ldx; q.B = W; q.ldb = ldw; q.M = M; q.N = N; q.K = K;
   q.D = Y; q.ldd = ldy; q.epi = TC_EPI_STORE;
+  return launch_tc_gemm(dt, q, as_stream(stream));
+}
+
+int ie_gemm_f32out(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, float* Y,
+                   int64_t ldy, void* stream) {
+  if (!valid_dtype(dt) || M < 0 || N < 0 || K <= 0) return IE_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return IE_OK;
+  if (K % 8) return IE_ERR_ALIGNMENT;
+  int s;
+  if ((s = check_matrix(X, ldx, K)) || (s = check_matrix(W, ldw, K))) return s;
+  if (!Y || ldy < N) return IE_ERR_INVALID_ARG;
+  if (M <= kSkinnyMaxM) {
+    SkinnyParams p;
+    p.X = X; p.ldx = ldx; p.M = M; p.N = N; p.K = K;
+    p.W0 = W; p.ldw = ldw; p.Y = Y; p.ldy = ldy;
+    return from_cuda(launch_skinny(dt, EPI_STORE_F32, p, as_stream(stream)));
+  }
+  if (!aligned16(Y) || (ldy % 4) != 0) return IE_ERR_ALIGNMENT;
+  TcGemmParams q;
+  q.A = X; q.lda = ldx; q.B = W; q.ldb = ldw; q.M = M; q.N = N; q.K = K;
+  q.D = Y; q.ldd = ldy; q.epi = TC_EPI_STORE_F32;
   return launch_tc_gemm(dt, q, as_stream(stream));
 }
 

@@ -1,9 +1,602 @@
-// Prefill-path GEMM (M > 16): tcgen05 / TMEM / TMA kernel.
+// Prefill-path GEMM (M > 16): D[M,N] = A[M,K] . B[N,K]^T on the sm_100a
+// tensor cores (tcgen05.mma kind::f16, fp32 accumulation in TMEM), fed by TMA.
+//
+// Roofline: at M = 2048 every projection of the hot path is compute-bound
+// (arithmetic intensity 1000+ FLOP/byte); the bound is the dense bf16
+// tensor-core peak. Algorithmic FLOPs per launch = 2*M*N*K.
+//
+// Design (one persistent CTA per SM, 192 threads, ~194 KB shared memory):
+//   warp 0, one lane  — TMA producer: per 64-wide k-block it loads the
+//                       128x64 activation tile and two 128x64 weight tiles
+//                       (128-byte swizzle) into a 4-stage ring;
+//   warp 1, one lane  — MMA issuer: four tcgen05.mma (M=128, N=256, K=16)
+//                       per k-block into one of two TMEM accumulators
+//                       (2 x 256 fp32 columns = all 512 TMEM columns), and
+//                       tcgen05.commit to release ring stages / publish
+//                       finished accumulators;
+//   warps 2..5        — epilogue: tcgen05.ld of the accumulator (thread =
+//                       output row), the fused epilogue, global stores; the
+//                       double-buffered accumulator lets the epilogue of one
+//                       tile overlap the main loop of the next.
+// The two 128-row weight tiles of a stage are independent TMA loads, which is
+// what lets the fused epilogues pair rows from different matrices:
+//   SWIGLU — gate rows [n0,n0+128) next to up rows [n0,n0+128);
+//   QKV    — two heads per tile, each taken from Wq, Wk or Wv;
+//   ARGMAX — 256 consecutive vocabulary rows.
+// No TMA multicast and no clusters: every load reads this GPU's own memory.
+//
+// Every mbarrier wait is bounded by the global timer; a wait that gives up
+// records IE_ERR_TIMEOUT in a device status word (ie_device_status()), makes
+// every role leave its loop, drains the copies and MMAs the CTA issued and
+// frees its TMEM before the CTA exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
 #include "ie_common.cuh"
 #include "gemm_tc.cuh"
 
 namespace ie {
 
-int launch_tc_gemm(ie_dtype, const TcGemmParams&, cudaStream_t) { return IE_ERR_UNSUPPORTED; }
+__device__ int g_tc_status = 0;
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_TILE = BM * BK * 2;     // 16 KB
+constexpr int B_HALF = 128 * BK * 2;    // 16 KB
+constexpr int STAGE_BYTES = A_TILE + 2 * B_HALF;
+constexpr int TILE_BYTES = STAGES * STAGE_BYTES;  // 192 KB
+constexpr int SMEM_BYTES = TILE_BYTES + 1024 + 256;
+constexpr int THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait
+
+struct TcArgs {
+  CUtensorMap tmA;
+  CUtensorMap tmB[3];
+  TcGemmParams p;
+  int nm, nn, nk;
+  int heads;  // QKV: n_q_heads + 2 * n_kv_heads
+};
+
+// ------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; false when it gave up (status recorded, abort raised) or
+// when another role already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitNs) {
+      atomicExch(&g_tc_status, IE_ERR_TIMEOUT);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major, 128-byte-swizzled operand tile: 8-row x 128-byte atoms stacked
+// every 1024 bytes (SBO), leading offset unused for swizzled K-major (1),
+// descriptor version 1 (sm_100), layout type 2 = SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)64 << 32) | ((uint64_t)1 << 46) |
+         ((uint64_t)2 << 61);
+}
+// kind::f16 instruction descriptor: fp32 accumulate, A/B same 16-bit type,
+// both K-major, N = 256, M = 128.
+template <typename T>
+__device__ __forceinline__ uint32_t idesc_f16() {
+  constexpr uint32_t fmt = DT<T>::id == IE_DTYPE_BF16 ? 1u : 0u;
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
+      "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Store 32 consecutive values of one output row (columns col0.. col0+31,
+// those < ncols), 16-byte vectors when the whole chunk is in range.
+template <typename T>
+__device__ __forceinline__ void store_row32(T* dst, int col0, int ncols, const float (&v)[32]) {
+  if (col0 + 32 <= ncols) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 pk;
+      T* e = reinterpret_cast<T*>(&pk);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) e[i] = DT<T>::from_f(v[j * 8 + i]);
+      *reinterpret_cast<uint4*>(dst + col0 + j * 8) = pk;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < ncols) dst[col0 + i] = DT<T>::from_f(v[i]);
+  }
+}
+
+// 32 fp32 values of one output row (tensor-parallel partial sums).
+__device__ __forceinline__ void store_row32_f32(float* dst, int col0, int ncols, const float (&v)[32]) {
+  if (col0 + 32 <= ncols) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<float4*>(dst + col0 + j * 4) = make_float4(v[j * 4], v[j * 4 + 1], v[j * 4 + 2], v[j * 4 + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < ncols) dst[col0 + i] = v[i];
+  }
+}
+
+// Which weight map / row feeds B half h of column block nb.
+template <int EPI>
+__device__ __forceinline__ void b_source(const TcArgs& a, int nb, int h, int& map, int& row) {
+  if constexpr (EPI == TC_EPI_SWIGLU) {
+    map = h;
+    row = nb * 128;
+  } else if constexpr (EPI == TC_EPI_QKV) {
+    int head = 2 * nb + h;
+    if (head >= a.heads) head = 2 * nb;  // odd head count: reload, result unused
+    if (head < a.p.n_q_heads) { map = 0; row = head * 128; }
+    else if (head < a.p.n_q_heads + a.p.n_kv_heads) { map = 1; row = (head - a.p.n_q_heads) * 128; }
+    else { map = 2; row = (head - a.p.n_q_heads - a.p.n_kv_heads) * 128; }
+  } else {
+    map = 0;
+    row = nb * BN + h * 128;
+  }
+}
+
+template <typename T, int EPI>
+__global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TILE_BYTES);
+  // bars: full[0..S), empty[S..2S), acc_full[2S..2S+2), acc_empty[2S+2..2S+4), drain[2S+4]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  int* issued_p = reinterpret_cast<int*>(tmem_holder + 2);
+  int* consumed_p = reinterpret_cast<int*>(tmem_holder + 3);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const TcGemmParams& p = args.p;
+  const int num_tiles = args.nm * args.nn;
+
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };
+  auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
+  auto accf_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + a); };
+  auto acce_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + 2 + a); };
+  const uint32_t drain_bar = smem_u32(bars + 2 * STAGES + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(accf_bar(a), 1);
+      mbar_init(acce_bar(a), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    *issued_p = 0;
+    *consumed_p = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&args.tmA)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  // Activations come from the previous kernel in the stream; outputs may be
+  // buffers it still reads.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      int stage = 0, issued = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        const int mb = tile % args.nm, nb = tile / args.nm;
+        for (int kb = 0; kb < args.nk; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag)) break;
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          mbar_expect_tx(full_bar(stage), STAGE_BYTES);
+          tma_load_2d(sa, &args.tmA, full_bar(stage), kb * BK, mb * BM);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            int map, row;
+            b_source<EPI>(args, nb, h, map, row);
+            tma_load_2d(sa + A_TILE + h * B_HALF, &args.tmB[map], full_bar(stage), kb * BK, row);
+          }
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      *issued_p = issued;
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      const uint32_t idesc = idesc_f16<T>();
+      int stage = 0, consumed = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool issued_any = false;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        if (!mbar_wait(acce_bar(acc), acc_phase ^ 1, abort_flag)) break;
+        fence_after();
+        const uint32_t d_tmem = tmem + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < args.nk; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
+          fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + A_TILE);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          mma_commit(empty_bar(stage));
+          issued_any = true;
+          ++consumed;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit(accf_bar(acc));
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      *consumed_p = consumed;
+      if (*abort_flag && issued_any) {
+        // let every MMA this thread issued finish before TMEM is released
+        mma_commit(drain_bar);
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_try(drain_bar, 0) && globaltimer() - t0 < kWaitNs) {
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------- epilogue warps
+    const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
+    const int row = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+      const int mb = tile % args.nm, nb = tile / args.nm;
+      if (!mbar_wait(accf_bar(acc), acc_phase, abort_flag)) break;
+      fence_after();
+      const uint32_t tbase = tmem + acc * BN + ((uint32_t)(quad * 32) << 16);
+      const int m = mb * BM + row;
+      const bool mvalid = m < p.M;
+      float v[32];
+      if constexpr (EPI == TC_EPI_STORE_F32) {
+        float* drow = static_cast<float*>(p.D) + (int64_t)m * p.ldd;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          tmem_ld32(tbase + c * 32, v);
+          if (mvalid) store_row32_f32(drow, nb * BN + c * 32, p.N, v);
+        }
+      } else if constexpr (EPI == TC_EPI_STORE) {
+        T* drow = static_cast<T*>(p.D) + (int64_t)m * p.ldd;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          tmem_ld32(tbase + c * 32, v);
+          if (mvalid) store_row32<T>(drow, nb * BN + c * 32, p.N, v);
+        }
+      } else if constexpr (EPI == TC_EPI_SWIGLU) {
+        T* drow = static_cast<T*>(p.D) + (int64_t)m * p.ldd;
+        float u[32];
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(tbase + c * 32, v);
+          tmem_ld32(tbase + 128 + c * 32, u);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float gv = round_to<T>(v[i]), uv = round_to<T>(u[i]);
+            v[i] = gv * (1.0f / (1.0f + expf(-gv))) * uv;
+          }
+          if (mvalid) store_row32<T>(drow, nb * 128 + c * 32, p.N, v);
+        }
+      } else if constexpr (EPI == TC_EPI_QKV) {
+        float b[32];
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          const int head = 2 * nb + h;
+          if (head >= args.heads) break;
+          T* dst;
+          bool rope;
+          const int pos = p.pos0 + m;
+          if (head < p.n_q_heads) {
+            dst = static_cast<T*>(p.q_out) + (int64_t)head * p.q_head_stride + (int64_t)m * 128;
+            rope = p.rope_cos != nullptr;
+          } else if (head < p.n_q_heads + p.n_kv_heads) {
+            dst = static_cast<T*>(p.k_cache) + (int64_t)(head - p.n_q_heads) * p.cache_head_stride +
+                  (int64_t)pos * 128;
+            rope = p.rope_cos != nullptr;
+          } else {
+            dst = static_cast<T*>(p.v_cache) + (int64_t)(head - p.n_q_heads - p.n_kv_heads) * p.cache_head_stride +
+                  (int64_t)pos * 128;
+            rope = false;
+          }
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            tmem_ld32(tbase + h * 128 + c * 32, v);       // d in [32c, 32c+32)
+            tmem_ld32(tbase + h * 128 + 64 + c * 32, b);  // d + 64
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              float x0 = round_to<T>(v[i]), x1 = round_to<T>(b[i]);
+              if (rope && mvalid) {
+                const int d = c * 32 + i;
+                const float cs = p.rope_cos[(int64_t)pos * 64 + d];
+                const float sn = p.rope_sin[(int64_t)pos * 64 + d];
+                const float y0 = x0 * cs - x1 * sn;
+                const float y1 = x0 * sn + x1 * cs;
+                x0 = y0;
+                x1 = y1;
+              }
+              v[i] = x0;
+              b[i] = x1;
+            }
+            if (mvalid) {
+              store_row32<T>(dst, c * 32, 128, v);
+              store_row32<T>(dst, 64 + c * 32, 128, b);
+            }
+          }
+        }
+      } else if constexpr (EPI == TC_EPI_ARGMAX) {
+        T* drow = p.D ? static_cast<T*>(p.D) + (int64_t)m * p.ldd : nullptr;
+        unsigned long long best = 0ull;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          tmem_ld32(tbase + c * 32, v);
+          const int col0 = nb * BN + c * 32;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            v[i] = round_to<T>(v[i]);
+            if (col0 + i < p.N) {
+              const unsigned long long k = argmax_key(v[i], p.vocab_offset + col0 + i);
+              best = k > best ? k : best;
+            }
+          }
+          if (mvalid && drow) store_row32<T>(drow, col0, p.N, v);
+        }
+        if (mvalid && best) atomicMax(p.keys + m, best);
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce_bar(acc));
+      if constexpr (EPI == TC_EPI_ARGMAX) {
+        // each epilogue warp counts its own part of the tile after its
+        // atomics; the warp that brings the count to 4 * tiles finalizes
+        if (lane == 0) {
+          __threadfence();
+          if (atomicAdd(p.counter, 1u) == 4u * (unsigned)num_tiles - 1u) {
+            __threadfence();
+            for (int r = 0; r < p.M; ++r) {
+              const unsigned long long k = atomicExch(p.keys + r, 0ull);
+              if (p.idx_out) p.idx_out[r] = argmax_key_index(k);
+              if (p.key_out) p.key_out[r] = k;
+            }
+            atomicExch(p.counter, 0u);
+          }
+        }
+      }
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  // ---------------------------------------------------------- teardown
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (*abort_flag && threadIdx.x == 0) {
+    // wait for TMA copies that were issued but never consumed
+    const int issued = *issued_p, consumed = *consumed_p;
+    for (int i = consumed; i < issued; ++i) {
+      const unsigned long long t0 = globaltimer();
+      while (!mbar_try(full_bar(i % STAGES), (uint32_t)((i / STAGES) & 1)) && globaltimer() - t0 < kWaitNs / 4) {
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+}
+
+// --------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// 2-D K-major tensor map: rows x K elements, row stride ld elements, box of
+// 64 x box_rows elements, 128-byte swizzle, zero fill outside the tensor.
+bool make_map(CUtensorMap* map, ie_dtype dt, const void* base, int rows, int K, int64_t ld, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUtensorMapDataType t = dt == IE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, t, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <typename T, int EPI>
+int launch_t(TcArgs& a, cudaStream_t st) {
+  static bool configured = false;
+  auto kernel = tc_gemm_kernel<T, EPI>;
+  if (!configured) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+      return IE_ERR_LAUNCH;
+    configured = true;
+  }
+  const int tiles = a.nm * a.nn;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles < sm_count() ? tiles : sm_count());
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, a);
+  if (e != cudaSuccess) {
+    std::fprintf(stderr, "infengine_b200: tcgen05 GEMM launch failed: %s\n", cudaGetErrorString(e));
+    return IE_ERR_LAUNCH;
+  }
+  return IE_OK;
+}
+
+template <typename T>
+int dispatch(TcArgs& a, int epi, cudaStream_t st) {
+  switch (epi) {
+    case TC_EPI_STORE: return launch_t<T, TC_EPI_STORE>(a, st);
+    case TC_EPI_SWIGLU: return launch_t<T, TC_EPI_SWIGLU>(a, st);
+    case TC_EPI_QKV: return launch_t<T, TC_EPI_QKV>(a, st);
+    case TC_EPI_ARGMAX: return launch_t<T, TC_EPI_ARGMAX>(a, st);
+    case TC_EPI_STORE_F32: return launch_t<T, TC_EPI_STORE_F32>(a, st);
+  }
+  return IE_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+int launch_tc_gemm(ie_dtype dt, const TcGemmParams& p, cudaStream_t st) {
+  if (p.M <= 0 || p.N <= 0 || p.K <= 0) return IE_OK;
+  TcArgs a;
+  memset(&a, 0, sizeof(a));
+  a.p = p;
+  a.nm = ceil_div(p.M, BM);
+  a.nk = ceil_div(p.K, BK);
+  if (!make_map(&a.tmA, dt, p.A, p.M, p.K, p.lda, BM)) return IE_ERR_UNSUPPORTED;
+  switch (p.epi) {
+    case TC_EPI_STORE:
+    case TC_EPI_STORE_F32:
+    case TC_EPI_ARGMAX:
+      a.nn = ceil_div(p.N, BN);
+      if (!make_map(&a.tmB[0], dt, p.B, p.N, p.K, p.ldb, 128)) return IE_ERR_UNSUPPORTED;
+      break;
+    case TC_EPI_SWIGLU:
+      a.nn = ceil_div(p.N, 128);
+      if (!make_map(&a.tmB[0], dt, p.B, p.N, p.K, p.ldb, 128) || !make_map(&a.tmB[1], dt, p.B2, p.N, p.K, p.ldb, 128))
+        return IE_ERR_UNSUPPORTED;
+      break;
+    case TC_EPI_QKV:
+      a.heads = p.n_q_heads + 2 * p.n_kv_heads;
+      a.nn = ceil_div(a.heads, 2);
+      if (!make_map(&a.tmB[0], dt, p.B, p.n_q_heads * 128, p.K, p.ldb, 128)) return IE_ERR_UNSUPPORTED;
+      if (p.n_kv_heads > 0) {
+        if (!make_map(&a.tmB[1], dt, p.B2, p.n_kv_heads * 128, p.K, p.ldb, 128) ||
+            !make_map(&a.tmB[2], dt, p.B3, p.n_kv_heads * 128, p.K, p.ldb, 128))
+          return IE_ERR_UNSUPPORTED;
+      } else {
+        a.tmB[1] = a.tmB[2] = a.tmB[0];
+      }
+      break;
+    default:
+      return IE_ERR_UNSUPPORTED;
+  }
+  return dt == IE_DTYPE_BF16 ? dispatch<__nv_bfloat16>(a, p.epi, st) : dispatch<__half>(a, p.epi, st);
+}
+
+int read_tc_status(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_tc_status, sizeof(int)) != cudaSuccess) return IE_ERR_LAUNCH;
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_tc_status, &z, sizeof(int));
+  }
+  return v;
+}
 
 }  // namespace ie

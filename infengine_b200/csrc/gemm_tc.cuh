@@ -11,6 +11,7 @@ enum TcEpilogue {
   TC_EPI_SWIGLU = 1,  // B = gate, B2 = up: D = round(silu(round(g)) * round(u))
   TC_EPI_ARGMAX = 2,  // logits (optional) + per-row packed-key argmax
   TC_EPI_QKV = 3,     // B/B2/B3 = Wq/Wk/Wv, head-major scatter + optional RoPE
+  TC_EPI_STORE_F32 = 4,  // D (float) [m, n] = acc, unrounded (tensor-parallel partial sums)
 };
 
 // D[M, N] = A[M, K] . B[N, K]^T (A = activations, B = weights, both K-major).
@@ -45,5 +46,8 @@ struct TcGemmParams {
 
 // Returns an IE_* status.
 int launch_tc_gemm(ie_dtype dt, const TcGemmParams& p, cudaStream_t st);
+
+// Device status word written by timed-out waits (IE_OK or IE_ERR_TIMEOUT).
+int read_tc_status(bool clear);
 
 }  // namespace ie

@@ -8,8 +8,9 @@
 //
 // Skinny GEMM design (one CTA = 16 weight rows, 8 warps split K):
 //  * each lane streams 16-byte chunks of two weight rows (g, g+8) with
-//    L1-bypassing, L2-evict-first loads, four 32-element k-steps per batch so
-//    every warp keeps 4-8 KB of weights in flight;
+//    L1-bypassing, L2-evict-first loads, two 32-element k-steps per batch,
+//    and issues its next batch before computing on the current one, so every
+//    warp keeps 2-4 KB of weights in flight at all times;
 //  * the dot products run on the tensor cores through m16n8k16: the weight
 //    tile is the A operand (16 rows) and the activation rows are the B
 //    operand (n = 8 batch rows; two n-tiles for M <= 16). The 8 elements a
@@ -20,6 +21,7 @@
 //    a fixed order (deterministic results), then one warp runs the epilogue.
 #include "ie_common.cuh"
 #include "skinny.cuh"
+#include <cstdlib>
 
 namespace ie {
 
@@ -49,7 +51,26 @@ template <> struct Mma<__nv_bfloat16> {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kUnroll = 4;  // 32-element k-steps whose loads are issued together
+// Build-time shape of the weight stream (one configuration is compiled in).
+// Chosen by an A/B on one B200 over the full decode step (129 launches, 15 GB):
+// 16-byte loads, 2 k-steps per batch, register double-buffering gave 2.79 ms;
+// 16 B x 4 without double-buffering 2.81 ms; 32-byte (v8) loads 2.90-3.43 ms;
+// persistent grids 3.18-3.36 ms.
+#ifndef IE_SK_LOADW
+#define IE_SK_LOADW 16   // bytes each lane loads per weight row per k-step (16 or 32)
+#endif
+#ifndef IE_SK_UNROLL
+#define IE_SK_UNROLL 2   // k-steps whose loads are issued together
+#endif
+#ifndef IE_SK_PIPE
+#define IE_SK_PIPE 1     // 1: next batch's loads issued before this batch's MMAs
+#endif
+#ifndef IE_SK_PERSIST
+#define IE_SK_PERSIST 0  // 1: resident CTAs walk the tiles with a grid stride
+#endif
+constexpr int kWords = IE_SK_LOADW / 4;  // 32-bit words per lane per row per k-step
+constexpr int kStep = kWords * 2 * 4;    // k elements per step (4 lanes share a row)
+constexpr int kUnroll = IE_SK_UNROLL;
 
 template <int EPI> struct EpiTraits { static constexpr int nmat = 1; };
 template <> struct EpiTraits<EPI_SWIGLU> { static constexpr int nmat = 2; };
@@ -79,101 +100,22 @@ __device__ __forceinline__ const T* weight_row(const SkinnyParams& p, int tile, 
   }
 }
 
+// Epilogues, run by warp 0 on the fully reduced tile.
+// acc[.][mt][i]: weight row g + 8*(i>>1) of the tile, batch row m = mt*8 + 2t + (i&1).
 template <typename T, int MT, int EPI>
-__global__ void __launch_bounds__(kThreads) skinny_kernel(const SkinnyParams p) {
-  constexpr int NMAT = EpiTraits<EPI>::nmat;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const int tile = blockIdx.x;
-
-  const T* wrow[NMAT][2];
-  bool rvalid[2];
-  int nidx[2];
-#pragma unroll
-  for (int mat = 0; mat < NMAT; ++mat)
-#pragma unroll
-    for (int r = 0; r < 2; ++r) wrow[mat][r] = weight_row<T, EPI>(p, tile, g + 8 * r, mat, rvalid[r], nidx[r]);
-
-  const T* xrow[MT];
-  bool xvalid[MT];
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt) {
-    const int m = mt * 8 + g;
-    xvalid[mt] = m < p.M;
-    xrow[mt] = static_cast<const T*>(p.X) + (int64_t)(xvalid[mt] ? m : 0) * p.ldx;
-  }
-
-  const int nsteps = (p.K + 31) >> 5;
-  const int s_begin = (warp * nsteps) / kWarps;
-  const int s_end = ((warp + 1) * nsteps) / kWarps;
-
-  float acc[NMAT][MT][4];
-#pragma unroll
-  for (int mat = 0; mat < NMAT; ++mat)
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[mat][mt][i] = 0.f;
-
-  const uint64_t pol = policy_evict_first();
-  const uint4 zero = make_uint4(0, 0, 0, 0);
-
-  for (int s = s_begin; s < s_end; s += kUnroll) {
-    uint4 wv[kUnroll][NMAT][2];
-    uint4 xv[kUnroll][MT];
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int k = (s + u) * 32 + t * 8;
-      const bool kv = (s + u < s_end) && (k < p.K);
-#pragma unroll
-      for (int mat = 0; mat < NMAT; ++mat)
-#pragma unroll
-        for (int r = 0; r < 2; ++r)
-          wv[u][mat][r] = (kv && rvalid[r]) ? ld_stream_v4(wrow[mat][r] + k, pol) : zero;
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) xv[u][mt] = (kv && xvalid[mt]) ? ld_act_v4(xrow[mt] + k) : zero;
-    }
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u)
-#pragma unroll
-      for (int mat = 0; mat < NMAT; ++mat)
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          // lane's 8 elements e0..e7 of rows g / g+8 / batch row g:
-          //   MMA 0 k-slots (2t,2t+1) <- e0,e1 ; (2t+8,2t+9) <- e2,e3
-          //   MMA 1 k-slots (2t,2t+1) <- e4,e5 ; (2t+8,2t+9) <- e6,e7
-          Mma<T>::run(acc[mat][mt], wv[u][mat][0].x, wv[u][mat][1].x, wv[u][mat][0].y, wv[u][mat][1].y,
-                      xv[u][mt].x, xv[u][mt].y);
-          Mma<T>::run(acc[mat][mt], wv[u][mat][0].z, wv[u][mat][1].z, wv[u][mat][0].w, wv[u][mat][1].w,
-                      xv[u][mt].z, xv[u][mt].w);
-        }
-  }
-
-  // ---- cross-warp reduction (fixed order) ----
-  constexpr int NR = NMAT * MT * 4;
-  __shared__ float red[kWarps][NR][32];
-#pragma unroll
-  for (int mat = 0; mat < NMAT; ++mat)
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) red[warp][(mat * MT + mt) * 4 + i][lane] = acc[mat][mt][i];
-  __syncthreads();
-  if (warp != 0) return;
-#pragma unroll
-  for (int mat = 0; mat < NMAT; ++mat)
+__device__ __forceinline__ void epilogue(const SkinnyParams& p, int tile, int g, int t, int lane,
+                                         const bool (&rvalid)[2], const int (&nidx)[2],
+                                         float (&acc)[EpiTraits<EPI>::nmat][MT][4]) {
+  if constexpr (EPI == EPI_STORE_F32) {
+    float* Y = static_cast<float*>(p.Y);
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        float s = 0.f;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) s += red[w][(mat * MT + mt) * 4 + i][lane];
-        acc[mat][mt][i] = s;
+        const int r = i >> 1, m = mt * 8 + 2 * t + (i & 1);
+        if (rvalid[r] && m < p.M) Y[(int64_t)m * p.ldy + nidx[r]] = acc[0][mt][i];
       }
-
-  // ---- epilogues. acc[.][mt][i]: row (g + 8*(i>>1)), batch m = mt*8 + 2t + (i&1)
-  if constexpr (EPI == EPI_STORE) {
+  } else if constexpr (EPI == EPI_STORE) {
     T* Y = static_cast<T*>(p.Y);
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
@@ -222,7 +164,7 @@ __global__ void __launch_bounds__(kThreads) skinny_kernel(const SkinnyParams p) 
     }
     __threadfence();
     unsigned int last = 0;
-    if (lane == 0) last = (atomicAdd(p.counter, 1u) == gridDim.x - 1) ? 1u : 0u;
+    if (lane == 0) last = (atomicAdd(p.counter, 1u) == p.tiles - 1) ? 1u : 0u;
     last = __shfl_sync(0xffffffffu, last, 0);
     if (last) {
       __threadfence();
@@ -267,6 +209,179 @@ __global__ void __launch_bounds__(kThreads) skinny_kernel(const SkinnyParams p) 
       }
   }
 }
+
+// One k-step chunk of a row for one lane: kLoadBytes (16 or 32) bytes = E
+// 32-bit words, starting at element k; zero past K (K % 8 == 0, so a 32-byte
+// chunk is full, half-full or empty). `wide` (row 32-byte aligned) allows
+// one 256-bit load; otherwise 128-bit loads.
+template <int E>
+__device__ __forceinline__ void ld_chunk(const void* row, int k, int K, bool valid, bool wide, bool stream,
+                                         uint64_t pol, uint32_t (&r)[E]) {
+  const char* a = static_cast<const char*>(row) + (int64_t)k * 2;
+  if constexpr (E == 8) {
+    if (valid && k + 16 <= K && wide) {
+      if (stream)
+        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8], %9;"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                     : "l"(a), "l"(pol));
+      else
+        asm volatile("ld.global.nc.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                     : "l"(a));
+      return;
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < E / 4; ++h) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (valid && k + 8 * (h + 1) <= K) v = stream ? ld_stream_v4(a + 16 * h, pol) : ld_act_v4(a + 16 * h);
+    r[4 * h] = v.x; r[4 * h + 1] = v.y; r[4 * h + 2] = v.z; r[4 * h + 3] = v.w;
+  }
+}
+
+// Registers of one load batch: kUnroll k-steps of two rows per weight matrix
+// and of the activation row(s).
+template <int NMAT, int MT>
+struct Batch {
+  uint32_t w[kUnroll][NMAT][2][kWords];
+  uint32_t x[kUnroll][MT][kWords];
+};
+
+// Grid = one CTA per 16-row tile (IE_SK_PERSIST = 0) or a persistent grid of
+// resident CTAs that walk the tiles with a grid stride. Inside a CTA the 8
+// warps split the K range of the tile; with IE_SK_PIPE each warp issues the
+// loads of its next batch before the MMAs of the current one, so it always
+// has loads in flight.
+template <typename T, int MT, int EPI>
+__global__ void __launch_bounds__(kThreads) skinny_kernel(const SkinnyParams p) {
+  constexpr int NMAT = EpiTraits<EPI>::nmat;
+  constexpr int NR = NMAT * MT * 4;
+  __shared__ float red[kWarps][NR][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+
+  const T* xrow[MT];
+  bool xvalid[MT];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    const int m = mt * 8 + g;
+    xvalid[mt] = m < p.M;
+    xrow[mt] = static_cast<const T*>(p.X) + (int64_t)(xvalid[mt] ? m : 0) * p.ldx;
+  }
+  const int nsteps = (p.K + kStep - 1) / kStep;
+  const int s_begin = (warp * nsteps) / kWarps;
+  const int s_end = ((warp + 1) * nsteps) / kWarps;
+  const uint64_t pol = policy_evict_first();
+
+  // Programmatic dependent launch: activations (X) come from the previous
+  // kernel and the outputs may be buffers it still reads, so nothing global
+  // is touched before this wait; the next kernel may be scheduled from here.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+#if IE_SK_PERSIST
+  for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
+#else
+  {
+    const int tile = blockIdx.x;
+#endif
+    const T* wrow[NMAT][2];
+    bool rvalid[2];
+    int nidx[2];
+#pragma unroll
+    for (int mat = 0; mat < NMAT; ++mat)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) wrow[mat][r] = weight_row<T, EPI>(p, tile, g + 8 * r, mat, rvalid[r], nidx[r]);
+
+    float acc[NMAT][MT][4];
+#pragma unroll
+    for (int mat = 0; mat < NMAT; ++mat)
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[mat][mt][i] = 0.f;
+
+    auto load = [&](Batch<NMAT, MT>& b, int s) {
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int k = (s + u) * kStep + t * (kWords * 2);
+        const bool kv = s + u < s_end;
+#pragma unroll
+        for (int mat = 0; mat < NMAT; ++mat)
+#pragma unroll
+          for (int r = 0; r < 2; ++r)
+            ld_chunk<kWords>(wrow[mat][r], k, p.K, kv && rvalid[r], p.w_wide, true, pol, b.w[u][mat][r]);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) ld_chunk<kWords>(xrow[mt], k, p.K, kv && xvalid[mt], p.x_wide, false, pol, b.x[u][mt]);
+      }
+    };
+    auto compute = [&](const Batch<NMAT, MT>& b) {
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+        for (int mat = 0; mat < NMAT; ++mat)
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int j = 0; j < kWords / 2; ++j) {
+              // lane's chunk e0.. of rows g / g+8 / batch row g: MMA j takes
+              // k-slots (2t,2t+1) <- e[4j],e[4j+1] and (2t+8,2t+9) <- e[4j+2],e[4j+3]
+              Mma<T>::run(acc[mat][mt], b.w[u][mat][0][2 * j], b.w[u][mat][1][2 * j], b.w[u][mat][0][2 * j + 1],
+                          b.w[u][mat][1][2 * j + 1], b.x[u][mt][2 * j], b.x[u][mt][2 * j + 1]);
+            }
+    };
+
+#if IE_SK_PIPE
+    {
+      Batch<NMAT, MT> b0, b1;
+      int s = s_begin;
+      if (s < s_end) load(b0, s);
+      while (s < s_end) {
+        if (s + kUnroll < s_end) load(b1, s + kUnroll);
+        compute(b0);
+        s += kUnroll;
+        if (s >= s_end) break;
+        if (s + kUnroll < s_end) load(b0, s + kUnroll);
+        compute(b1);
+        s += kUnroll;
+      }
+    }
+#else
+    for (int s = s_begin; s < s_end; s += kUnroll) {
+      Batch<NMAT, MT> b;
+      load(b, s);
+      compute(b);
+    }
+#endif
+
+    // ---- cross-warp reduction (fixed order) ----
+#pragma unroll
+    for (int mat = 0; mat < NMAT; ++mat)
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) red[warp][(mat * MT + mt) * 4 + i][lane] = acc[mat][mt][i];
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+      for (int mat = 0; mat < NMAT; ++mat)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float sum = 0.f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) sum += red[w][(mat * MT + mt) * 4 + i][lane];
+            acc[mat][mt][i] = sum;
+          }
+      epilogue<T, MT, EPI>(p, tile, g, t, lane, rvalid, nidx, acc);
+    }
+#if IE_SK_PERSIST
+    __syncthreads();  // red is reused by the next tile
+#endif
+  }
+}
+
 
 // ------------------------------------------------------------------ SwiGLU
 template <typename T>
@@ -361,11 +476,67 @@ __global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmax
 }  // namespace
 
 // ------------------------------------------------------------------ launchers
+// Launches with programmatic stream serialization, so the kernel may start
+// while its predecessor drains (see the griddepcontrol notes in the kernel).
+// IE_PDL=0 in the environment turns it off (plain stream ordering).
+static bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("IE_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename K, typename... Args>
+static cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+static bool rows_wide(const void* base, int64_t ld) {
+  return (reinterpret_cast<uintptr_t>(base) & 31u) == 0 && (ld % 16) == 0;
+}
+
+// Persistent grids: as many CTAs as fit on the device at once.
+template <typename K>
+static int resident_ctas(K kernel) {
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0);
+  return (sms > 0 ? sms : 148) * (per_sm > 0 ? per_sm : 1);
+}
+
+template <typename T, int MT, int EPI>
+static cudaError_t launch_variant(const SkinnyParams& p, cudaStream_t st) {
+  auto kernel = skinny_kernel<T, MT, EPI>;
+  int grid = p.tiles;
+#if IE_SK_PERSIST
+  static const int resident = resident_ctas(kernel);
+  grid = p.tiles < resident ? p.tiles : resident;
+#endif
+  return launch_pdl(kernel, dim3(grid), dim3(kThreads), st, p);
+}
+
 template <typename T, int EPI>
-static cudaError_t launch_skinny_t(const SkinnyParams& p, int tiles, cudaStream_t st) {
-  if (p.M <= 8) skinny_kernel<T, 1, EPI><<<tiles, kThreads, 0, st>>>(p);
-  else skinny_kernel<T, 2, EPI><<<tiles, kThreads, 0, st>>>(p);
-  return cudaGetLastError();
+static cudaError_t launch_skinny_t(const SkinnyParams& p0, int tiles, cudaStream_t st) {
+  SkinnyParams p = p0;
+  constexpr int nmat = EpiTraits<EPI>::nmat;
+  p.tiles = tiles;
+  p.w_wide = rows_wide(p.W0, p.ldw) && (nmat < 2 || rows_wide(p.W1, p.ldw)) &&
+             (EPI != EPI_QKV || p.n_kv_heads == 0 || (rows_wide(p.W1, p.ldw) && rows_wide(p.W2, p.ldw)));
+  p.x_wide = rows_wide(p.X, p.ldx);
+  if (p.M <= 8) return launch_variant<T, 1, EPI>(p, st);
+  return launch_variant<T, 2, EPI>(p, st);
 }
 
 cudaError_t launch_skinny(ie_dtype dt, int epi, const SkinnyParams& p, cudaStream_t st) {
@@ -379,6 +550,7 @@ cudaError_t launch_skinny(ie_dtype dt, int epi, const SkinnyParams& p, cudaStrea
     case EPI_SWIGLU: return launch_skinny_t<T, EPI_SWIGLU>(p, tiles, st); \
     case EPI_ARGMAX: return launch_skinny_t<T, EPI_ARGMAX>(p, tiles, st); \
     case EPI_QKV: return launch_skinny_t<T, EPI_QKV>(p, tiles, st);      \
+    case EPI_STORE_F32: return launch_skinny_t<T, EPI_STORE_F32>(p, tiles, st); \
   }
   if (dt == IE_DTYPE_F16) { IE_SK(__half) }
   else { IE_SK(__nv_bfloat16) }

@@ -11,6 +11,7 @@ enum SkinnyEpilogue {
   EPI_SWIGLU = 1,  // two matrices (gate = W0, up = W1): Y = round(silu(round(g)) * round(u))
   EPI_ARGMAX = 2,  // logits (optional store) + packed-key argmax per batch row
   EPI_QKV = 3,     // head-major scatter of Q / K-cache / V-cache rows, optional RoPE
+  EPI_STORE_F32 = 4,  // Y (float) [m, n] = acc, unrounded (tensor-parallel partial sums)
 };
 
 struct SkinnyParams {
@@ -21,6 +22,9 @@ struct SkinnyParams {
   const void* W1 = nullptr;
   const void* W2 = nullptr;
   int64_t ldw = 0;
+  // set by launch_skinny: all weight / activation rows 32-byte aligned; tile count
+  bool w_wide = false, x_wide = false;
+  int tiles = 0;
   void* Y = nullptr;
   int64_t ldy = 0;
   // EPI_ARGMAX

@@ -176,12 +176,16 @@ def argmax_reference(logits: np.ndarray, threads: int = 1024) -> int:
     replacing on a strictly greater value (:36-45); then a shared-memory
     tree keeps [i] unless [i+delta] is strictly greater (:16-24). The
     comparisons follow IEEE semantics, so NaNs never win a comparison.
+
+    With fewer than `threads` logits the reference reads past the buffer
+    (every thread starts at logits[t]); here those threads hold -inf, which
+    is the rule infengine_b200 applies.
     """
     v = np.asarray(logits, dtype=np.float32).ravel()
     n = v.size
-    loc_val = np.empty(threads, dtype=np.float32)
-    loc_idx = np.empty(threads, dtype=np.int64)
-    for t in range(threads):
+    loc_val = np.full(threads, -np.inf, dtype=np.float32)
+    loc_idx = np.arange(threads, dtype=np.int64)
+    for t in range(min(threads, n)):
         col = v[t::threads]
         best_v, best_i = col[0], t
         # strict '>' scan, first occurrence of a new maximum wins

@@ -17,6 +17,18 @@ pytestmark = pytest.mark.gpu
 DTS = ["bf16", "f16"]
 
 
+def rope_tol(x, wq, wk, wv, dt, rope):
+    """Per-element bound for Q/K/V after RoPE: the rotation of a stored pair
+    (a, b) can cancel, so the error is bounded by the pair's magnitude
+    |a| + |b| (two rounding steps at that scale), not by the output's."""
+    out = []
+    for w, rot in ((wq, rope), (wk, rope), (wv, False)):
+        pre = np.abs(oracle.gemm_fp32(x, w)).reshape(x.shape[0], -1, 128).transpose(1, 0, 2)
+        mag = pre + np.concatenate([pre[..., 64:], pre[..., :64]], axis=-1) if rot else pre
+        out.append(2 * ulp(mag, dt) + 1e-5 * mag.max())
+    return out
+
+
 def assert_within_one_rounding(got, gold_fp32, dt):
     scale = float(np.abs(gold_fp32).max()) if gold_fp32.size else 0.0
     err = np.abs(got.astype(np.float64) - gold_fp32.astype(np.float64))
@@ -117,9 +129,10 @@ def test_qkv_fused(ie, cuda, dt, M, pos0, rope):
     got_q = from_dev(q)
     got_k = from_dev(kc)[:, pos0:pos0 + M]
     got_v = from_dev(vc)[:, pos0:pos0 + M]
-    for got, want in ((got_q, qr), (got_k, kr), (got_v, vr)):
-        tol = 2 * ulp(want, dt) + 1e-3 * np.abs(want).max()
-        assert np.all(np.abs(got - want) <= tol)
+    for got, want, tol in zip((got_q, got_k, got_v), (qr, kr, vr),
+                              rope_tol(d["x"], d["wq"], d["wk"], d["wv"], dt, rope)):
+        err = np.abs(got - want)
+        assert np.all(err <= tol), f"max err {err.max():.3g}, worst excess {(err - tol).max():.3g}"
     # no cache row outside [pos0, pos0+M) was touched
     kall = from_dev(kc)
     mask = np.ones(ctx, bool)
@@ -222,8 +235,11 @@ def test_argmax_tie_vectors(ie, cuda, dt):
         out = cuda.full((2,), -1, dtype=cuda.int32, device="cuda")
         ie.argmax(t[:, :V], out)
         got = out.cpu().numpy()
+        # rows shorter than 1024 have no reference behaviour (it reads past the
+        # buffer); the oracle then gives absent threads -inf, as the kernel does
         assert got[0] == oracle.argmax_reference(v)
         assert got[1] == oracle.argmax_reference(v[::-1].copy())
+        assert got[0] == oracle.argmax_reference_fast(v)
 
 
 @pytest.mark.parametrize("dt", DTS)

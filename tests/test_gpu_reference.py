@@ -46,9 +46,24 @@ def test_multiply_by_weight_vs_reference(ie, cuda, m, k, n):
     ie.multiply_by_weight(m, k, n, x, w, y_ie)
     cuda.cuda.synchronize()
     a, b = from_dev(y_ie), from_dev(y_ref)
-    # both round an fp32 accumulation: at most one rounding step apart
-    assert np.all(np.abs(a - b) <= ulp(np.maximum(np.abs(a), np.abs(b)), "f16") * 1.01 + 1e-6)
-    assert np.mean(a == b) > 0.9
+    gold = oracle.gemm_fp32(d["x"], d["w"])
+    err_ie = rounding_steps(a, gold)
+    err_ref = rounding_steps(b, gold)
+    # ours: one rounding of an fp32 accumulation (<= 1 step from exact). cuBLAS
+    # is called with CUBLAS_DEFAULT_MATH, which permits reduced-precision
+    # split-K reductions for fp16 output, so the reference may be further off.
+    assert err_ie.max() <= 1.0, f"ours {err_ie.max():.2f} steps from exact"
+    assert err_ie.max() <= max(err_ref.max(), 1.0)
+    assert oracle.max_rel_err(a, gold) <= 1e-2 and oracle.max_rel_err(b, gold) <= 1e-2
+    print(f"m={m} k={k} n={n}: ours max {err_ie.max():.2f} steps, reference max {err_ref.max():.2f} steps, "
+          f"equal outputs {np.mean(a == b):.4f}")
+
+
+def rounding_steps(actual, gold_fp32, dt="f16"):
+    """|actual - exact| in units of the storage type's spacing at the exact
+    value (fp16), with an absolute floor for cancellations near zero."""
+    scale = np.abs(gold_fp32).max()
+    return np.abs(actual.astype(np.float64) - gold_fp32) / (ulp(gold_fp32, dt) + 1e-5 * scale)
 
 
 @pytest.mark.parametrize("M", [1, 4, 8])
@@ -94,8 +109,14 @@ def test_lm_head_and_sampling_vs_reference(ie, cuda):
         ie.lm_head_argmax(x[S - 1:S], w, ws, idx_out=t_fused)
         cuda.cuda.synchronize()
         a, b = from_dev(l_ie), from_dev(l_ref)
-        assert np.all(np.abs(a - b) <= ulp(np.maximum(np.abs(a), np.abs(b)), "f16") * 1.01 + 1e-6)
+        gold = oracle.gemm_fp32(d["x"][S - 1:S], d["w"])[0]
+        assert rounding_steps(a, gold).max() <= 1.0
+        assert oracle.max_rel_err(b, gold) <= 1e-2
         assert int(t_fused.item()) == int(t_ie.item())
+        # ids agree with the reference unless its logits differ from ours at the top
+        if int(t_ie.item()) != int(t_ref.item()):
+            top = np.sort(gold)[-2:]
+            assert top[1] - top[0] <= 4 * ulp(top[1:], "f16")[0]
         # same sampler on the reference's logits gives the reference's token
         ie.sample_token_amax(l_ref, t_ie)
         cuda.cuda.synchronize()
