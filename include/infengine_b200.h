@@ -160,6 +160,29 @@ int ie_lm_head_argmax(ie_dtype dt, int M, int K, int V, int64_t vocab_offset,
                       int* idx_out, unsigned long long* key_out,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- allocation-free lm_head + argmax ---------------------------------------
+ * No counterpart in the reference. Same computation and outputs as
+ * ie_lm_head_argmax, for callers that cannot hand the library a workspace:
+ * code written against the reference's signatures (lm_head and
+ * sample_token_amax take none), processes whose device memory belongs to a
+ * pool allocator, and decode loops that must not call cudaMalloc/cudaFree
+ * because those can synchronize the device.
+ * It allocates nothing: its scratch (one key per row + a counter) is a fixed
+ * 768-byte array declared by the library in device memory, held by every GPU
+ * that loads the library until the process exits.
+ *   - M is at most 64; larger M returns IE_ERR_UNSUPPORTED.
+ *   - All calls share that array: calls whose kernels overlap on the GPU
+ *     (other streams or host threads on the same device) race. Each call
+ *     clears the array on its stream before launching.
+ *   - The first call on a device looks up the array's device address with
+ *     that device current; make that first call before any stream capture
+ *     begins.
+ */
+int ie_lm_head_argmax_noalloc(ie_dtype dt, int M, int K, int V, int64_t vocab_offset,
+                              const void* x, int64_t ldx, const void* W,
+                              void* logits, int64_t ld_logits,
+                              int* idx_out, unsigned long long* key_out, void* stream);
+
 /* ---- a7: argmax over stored logits ----------------------------------------
  * Replaces sample_token_amax (kernels/sampling.cu:54-58, sampling.cuh:4) for
  * M rows of V logits (row stride ld). Same tie rule as above. Needs no

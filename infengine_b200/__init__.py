@@ -53,6 +53,7 @@ STATUS = {
 EXPORTED_SYMBOLS = (
     "ie_status_string", "ie_version", "ie_gemm", "ie_swiglu", "ie_ffn_workspace_size", "ie_ffn", "ie_ffn_gate_up",
     "ie_qkv", "ie_lm_head_argmax_workspace_size", "ie_lm_head_argmax", "ie_argmax", "ie_device_status",
+    "ie_lm_head_argmax_noalloc",
 )
 
 
@@ -90,6 +91,8 @@ def lib() -> ctypes.CDLL:
         L.ie_lm_head_argmax_workspace_size.argtypes = [i32]
         L.ie_lm_head_argmax.argtypes = [i32, i32, i32, i32, i64, vp, i64, vp, vp, i64, vp, vp, vp, sz, vp]
         L.ie_argmax.argtypes = [i32, i32, i32, vp, i64, vp, vp]
+        L.ie_lm_head_argmax_noalloc.argtypes = [i32, i32, i32, i32, i64, vp, i64, vp, vp, i64, vp, vp, vp]
+        L.ie_lm_head_argmax_noalloc.restype = i32
         for name in ("ie_gemm", "ie_swiglu", "ie_ffn", "ie_qkv", "ie_lm_head_argmax", "ie_argmax"):
             getattr(L, name).restype = i32
         _lib_handle = L
@@ -183,6 +186,18 @@ def lm_head_argmax(x, w, workspace, logits=None, idx_out=None, key_out=None, voc
                                    ld_logits, _ptr(idx_out), _ptr(key_out), _ptr(workspace),
                                    workspace.numel() * workspace.element_size(), _stream(stream)),
            "ie_lm_head_argmax")
+
+
+def lm_head_argmax_noalloc(x, w, logits=None, idx_out=None, key_out=None, vocab_offset=0, stream=None):
+    """ie_lm_head_argmax_noalloc: lm_head + greedy id without a caller workspace
+    (at most 64 rows; calls overlapping on the GPU race on the library's
+    fixed scratch)."""
+    M, K = x.shape
+    V = w.shape[0]
+    ld_logits = logits.stride(0) if logits is not None else 0
+    _check(lib().ie_lm_head_argmax_noalloc(_dt(x), M, K, V, vocab_offset, _ptr(x), x.stride(0), _ptr(w),
+                                           _ptr(logits), ld_logits, _ptr(idx_out), _ptr(key_out), _stream(stream)),
+           "ie_lm_head_argmax_noalloc")
 
 
 def argmax(logits, idx_out, stream=None):
