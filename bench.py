@@ -145,26 +145,27 @@ def make_weights(torch, dev, dtype, seed: int):
 
 # ---------------------------------------------------------------- our arm
 class OursStep:
-    def __init__(self, torch, dev, seed):
+    def __init__(self, torch, dev, seed, batch: int = 1, layers=None):
         import infengine_b200 as ie
         from infengine_b200.host import rope_tables
         self.ie, self.torch = ie, torch
         dt = torch.bfloat16
-        self.layers, self.lm = make_weights(torch, dev, dt, seed)
+        self.M = batch
+        self.layers, self.lm = layers if layers is not None else make_weights(torch, dev, dt, seed)
         g = torch.Generator(device=dev)
         g.manual_seed(seed + 1)
-        self.x = torch.randn(1, H, generator=g, device=dev, dtype=torch.float32).to(dt)
-        self.q = torch.empty(NQ, 1, HD, device=dev, dtype=dt)
-        self.attn_out = torch.empty(1, H, device=dev, dtype=dt)
-        self.h = torch.empty(1, F, device=dev, dtype=dt)
-        self.ffn_out = torch.empty(1, H, device=dev, dtype=dt)
+        self.x = torch.randn(batch, H, generator=g, device=dev, dtype=torch.float32).to(dt)
+        self.q = torch.empty(NQ, batch, HD, device=dev, dtype=dt)
+        self.attn_out = torch.empty(batch, H, device=dev, dtype=dt)
+        self.h = torch.empty(batch, F, device=dev, dtype=dt)
+        self.ffn_out = torch.empty(batch, H, device=dev, dtype=dt)
         self.kc = torch.zeros(L, NKV, CTX, HD, device=dev, dtype=dt)
         self.vc = torch.zeros(L, NKV, CTX, HD, device=dev, dtype=dt)
         cos, sin = rope_tables(CTX)
         self.cos = torch.from_numpy(cos).to(dev)
         self.sin = torch.from_numpy(sin).to(dev)
-        self.ws = torch.zeros(ie.lm_head_workspace_bytes(1), dtype=torch.uint8, device=dev)
-        self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.ws = torch.zeros(ie.lm_head_workspace_bytes(batch), dtype=torch.uint8, device=dev)
+        self.tok = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.launches_per_step = L * 4 + 1
 
     def __call__(self):
@@ -172,7 +173,8 @@ class OursStep:
         for l, w in enumerate(self.layers):
             ie.qkv(self.x, w["wq"], w["wk"], w["wv"], self.q, self.kc[l], self.vc[l], CTX * HD, POS, self.cos,
                    self.sin)
-            ie.gemm(self.q.view(1, H), w["wo"], self.attn_out)
+            # stand-in for the attention output: the Q rows ([heads, M, 128] read as [M, 4096])
+            ie.gemm(self.q.view(self.M, H), w["wo"], self.attn_out)
             ie.ffn_gate_up(self.x, w["wg"], w["wu"], self.h)
             ie.gemm(self.h, w["wd"], self.ffn_out)
         ie.lm_head_argmax(self.x, self.lm, self.ws, idx_out=self.tok)
@@ -433,7 +435,7 @@ def main():
     if world > 1:
         from datetime import timedelta
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
 
@@ -594,6 +596,28 @@ def main():
             "gpu_launches": 4 * L,
         }
         del gp
+        # BASELINE config 5 shapes of the same path: batch-8 decode and the M=5
+        # verify pass (4 draft tokens + 1), same weights, one graph per step
+        for name, m in (("decode_bs8", 8), ("verify_m5", 5)):
+            sb = OursStep(torch, dev, args.seed, batch=m, layers=(step.layers, step.lm))
+            gb = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                sb()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(gb, stream=stream):
+                sb()
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    gb.replay()
+                ev0.record(stream)
+                for _ in range(10):
+                    gb.replay()
+                ev1.record(stream)
+            torch.cuda.synchronize()
+            ms_b = ev0.elapsed_time(ev1) / 10
+            result[name] = {"rows": m, "ms_per_step": round(ms_b, 4), "tok_per_s": round(m / (ms_b / 1e3), 1),
+                            "hbm_gbs": round(WEIGHT_BYTES / (ms_b / 1e3) / 1e9, 1)}
+            del gb, sb
         if rank == 0 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(args.seed)
     elif args.impl == "reference":
@@ -605,7 +629,12 @@ def main():
 
     if rank == 0:
         print(json.dumps(result), flush=True)
-    del graph  # graphs holding NCCL work go before the communicators
+    # graphs holding NCCL work are released before the communicators
+    run = None
+    if graph is not None:
+        graph.reset()
+    del graph
+    torch.cuda.synchronize()
     if hasattr(step, "close"):
         step.close()
     if world > 1:

@@ -137,6 +137,22 @@ int ie_qkv(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_di
            const float* rope_cos, const float* rope_sin,
            void* stream);
 
+/* ---- attention core behind the drop-in attn / decode_attn ---------------
+ * Replaces the score / softmax / value steps of attn and decode_attn
+ * (kernels/attn.cu:355-366 and :423-431, kernels/softmax.cu:55-160,
+ * kernels/attn_permute.cu:15-32). Causal grouped-query attention of S query
+ * rows at positions pos0 .. pos0+S-1 over cache rows 0 .. pos0+S-1:
+ *   q      [n_q_heads][S][128] (head stride q_head_stride), as ie_qkv writes it;
+ *   caches [n_kv_heads][.][128] (head stride cache_head_stride);
+ *   out    [S][n_q_heads*128] (row stride ld_out), the input of the O projection.
+ * Scores are rounded to dt, scaled by rsqrt(128) and rounded, softmaxed with
+ * the reference's roundings; head_dim 128, n_q_heads / n_kv_heads <= 8,
+ * (pos0 + S) * group <= ~50k (scores of a row are kept on chip). */
+int ie_attention(ie_dtype dt, int S, int pos0, int n_q_heads, int n_kv_heads, int head_dim,
+                 const void* q, int64_t q_head_stride,
+                 const void* k_cache, const void* v_cache, int64_t cache_head_stride,
+                 void* out, int64_t ld_out, void* stream);
+
 /* ---- a6 + a7: lm_head with fused greedy argmax --------------------------
  * Replaces lm_head (kernels/lm_head.cu:5-20) followed by sample_token_amax
  * (kernels/sampling.cu:54-58), for M rows at once.

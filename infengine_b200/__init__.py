@@ -53,7 +53,7 @@ STATUS = {
 EXPORTED_SYMBOLS = (
     "ie_status_string", "ie_version", "ie_gemm", "ie_swiglu", "ie_ffn_workspace_size", "ie_ffn", "ie_ffn_gate_up",
     "ie_qkv", "ie_lm_head_argmax_workspace_size", "ie_lm_head_argmax", "ie_argmax", "ie_device_status",
-    "ie_lm_head_argmax_noalloc",
+    "ie_lm_head_argmax_noalloc", "ie_attention",
 )
 
 
@@ -91,6 +91,8 @@ def lib() -> ctypes.CDLL:
         L.ie_lm_head_argmax_workspace_size.argtypes = [i32]
         L.ie_lm_head_argmax.argtypes = [i32, i32, i32, i32, i64, vp, i64, vp, vp, i64, vp, vp, vp, sz, vp]
         L.ie_argmax.argtypes = [i32, i32, i32, vp, i64, vp, vp]
+        L.ie_attention.argtypes = [i32, i32, i32, i32, i32, i32, vp, i64, vp, vp, i64, vp, i64, vp]
+        L.ie_attention.restype = i32
         L.ie_lm_head_argmax_noalloc.argtypes = [i32, i32, i32, i32, i64, vp, i64, vp, vp, i64, vp, vp, vp]
         L.ie_lm_head_argmax_noalloc.restype = i32
         for name in ("ie_gemm", "ie_swiglu", "ie_ffn", "ie_qkv", "ie_lm_head_argmax", "ie_argmax"):
@@ -172,6 +174,14 @@ def qkv(x, wq, wk, wv, q_out, k_cache, v_cache, cache_head_stride, pos0=0, rope_
     _check(lib().ie_qkv(_dt(x), M, H, n_q_heads, n_kv_heads, head_dim, _ptr(x), _ptr(wq), _ptr(wk), _ptr(wv),
                         _ptr(q_out), _ptr(k_cache), _ptr(v_cache), cache_head_stride, pos0, _ptr(rope_cos),
                         _ptr(rope_sin), _stream(stream)), "ie_qkv")
+
+
+def attention(q, k_cache, v_cache, out, pos0, n_kv_heads=NUM_KV_HEADS, stream=None):
+    """ie_attention: causal GQA over the cache; q [nq, S, 128] head-major,
+    caches [nkv, ctx, 128], out [S, nq*128]."""
+    nq, S, D = q.shape
+    _check(lib().ie_attention(_dt(q), S, pos0, nq, n_kv_heads, D, _ptr(q), q.stride(0), _ptr(k_cache), _ptr(v_cache),
+                              k_cache.stride(0), _ptr(out), out.stride(0), _stream(stream)), "ie_attention")
 
 
 def lm_head_workspace_bytes(M: int) -> int:

@@ -18,6 +18,7 @@
 #include "../../include/kernels/swiglu.cuh"
 #include "../../include/kernels/lm_head.cuh"
 #include "../../include/kernels/sampling.cuh"
+#include "../../include/kernels/attn.cuh"
 
 #define IE_DROPIN_EXPORT __attribute__((visibility("default")))
 
@@ -72,4 +73,57 @@ IE_DROPIN_EXPORT void lm_head(cublasHandle_t handle, const int seq_len, half* d_
 IE_DROPIN_EXPORT void sample_token_amax(const half* d_logits, int* d_output) {
   report(ie_argmax(IE_DTYPE_F16, 1, ie_llama::kVocabSize, d_logits, ie_llama::kVocabSize, d_output, nullptr),
          "sample_token_amax");
+}
+
+// ------------------------------------------------------------------ attention
+namespace {
+
+constexpr int64_t kCacheHeadStride = (int64_t)ie_llama::kMaxContextLength * ie_llama::kHeadDim;
+constexpr int64_t kLayerCacheElems = 2 * ie_llama::kNumKvHeads * kCacheHeadStride;
+
+// Q/K/V (+RoPE) into the workspace and the layer's cache rows, attention core,
+// O projection. Workspace: Q [32][S][128] then the attention output [S][4096].
+void attention_block(cublasHandle_t handle, const float* cos, const float* sin, int S, int pos0, const half* in,
+                     const half* wq, const half* wk, const half* wv, const half* wo, half* out, void* workspace,
+                     void* kv_cache, int layer_idx, const char* what) {
+  void* st = stream_of(handle);
+  half* q = static_cast<half*>(workspace);
+  half* ao = q + (size_t)S * ie_llama::kHiddenSize;
+  half* k_cache = static_cast<half*>(kv_cache) + (size_t)layer_idx * kLayerCacheElems;
+  half* v_cache = k_cache + ie_llama::kNumKvHeads * kCacheHeadStride;
+  int s = ie_qkv(IE_DTYPE_F16, S, ie_llama::kHiddenSize, ie_llama::kNumQHeads, ie_llama::kNumKvHeads,
+                 ie_llama::kHeadDim, in, wq, wk, wv, q, k_cache, v_cache, kCacheHeadStride, pos0, cos, sin, st);
+  if (s == IE_OK)
+    s = ie_attention(IE_DTYPE_F16, S, pos0, ie_llama::kNumQHeads, ie_llama::kNumKvHeads, ie_llama::kHeadDim, q,
+                     (int64_t)S * ie_llama::kHeadDim, k_cache, v_cache, kCacheHeadStride, ao, ie_llama::kHiddenSize,
+                     st);
+  if (s == IE_OK)
+    s = ie_gemm(IE_DTYPE_F16, S, ie_llama::kHiddenSize, ie_llama::kHiddenSize, ao, ie_llama::kHiddenSize, wo,
+                ie_llama::kHiddenSize, out, ie_llama::kHiddenSize, st);
+  report(s, what);
+}
+
+}  // namespace
+
+IE_DROPIN_EXPORT size_t attn_workspace_size(int max_seq_len) {
+  return 2 * (size_t)max_seq_len * ie_llama::kHiddenSize * sizeof(half);
+}
+
+IE_DROPIN_EXPORT size_t kv_cache_size() {
+  return (size_t)ie_llama::kNumLayers * kLayerCacheElems * sizeof(half);
+}
+
+IE_DROPIN_EXPORT void attn(cublasHandle_t handle, const float* d_rope_cos, const float* d_rope_sin, const int seq_len,
+                           half* d_input, half* d_qproj, half* d_kproj, half* d_vproj, half* d_oproj, half* d_output,
+                           void* workspace, void* kv_cache, const int layer_idx) {
+  attention_block(handle, d_rope_cos, d_rope_sin, seq_len, 0, d_input, d_qproj, d_kproj, d_vproj, d_oproj, d_output,
+                  workspace, kv_cache, layer_idx, "attn");
+}
+
+IE_DROPIN_EXPORT void decode_attn(cublasHandle_t handle, const float* d_rope_cos, const float* d_rope_sin,
+                                  const int seq_len, half* d_input, half* d_qproj, half* d_kproj, half* d_vproj,
+                                  half* d_oproj, half* d_output, void* workspace, void* kv_cache,
+                                  const int layer_idx) {
+  attention_block(handle, d_rope_cos, d_rope_sin, 1, seq_len - 1, d_input, d_qproj, d_kproj, d_vproj, d_oproj,
+                  d_output, workspace, kv_cache, layer_idx, "decode_attn");
 }

@@ -331,3 +331,31 @@ def qkv_cpu(x, wq, wk, wv, dt: str, pos0: int = 0, cos=None, sin=None, head_dim:
 def lm_head_argmax_cpu(x, w, dt: str):
     logits = gemm_cpu(x, w, dt)
     return logits, np.array([argmax_reference_fast(r) for r in logits], dtype=np.int64)
+
+
+# ------------------------------------------------ attention (drop-in core)
+def attention(q, k, v, pos0: int, dt: str):
+    """Causal grouped-query attention as the reference's attn / decode_attn
+    chain computes it (kernels/attn.cu:355-366, :423-431;
+    kernels/softmax.cu:55-160): scores = round(q.k) (the cuBLAS QK^T output),
+    t = round(score * rsqrt(128)), e = exp(t - max t) summed in fp32 and stored
+    rounded, p = round(round(e) * (1/sum)), out = round(p.V) (cuBLAS A.V).
+    q [nq, S, 128] (positions pos0..pos0+S-1), k/v [nkv, >= pos0+S, 128].
+    Returns the token-major [S, nq*128] output (attn_permute's layout)."""
+    nq, S, D = q.shape
+    nkv = k.shape[0]
+    group = nq // nkv
+    scale = np.float32(1.0 / math.sqrt(D))
+    out = np.zeros((S, nq * D), dtype=np.float32)
+    for h in range(nq):
+        hk = h // group
+        for s in range(S):
+            L = pos0 + s + 1
+            sc = round_dt((q[h, s].astype(np.float64) @ k[hk, :L].astype(np.float64).T).astype(np.float32), dt)
+            t = round_dt(sc * scale, dt)
+            e = np.exp(t - t.max()).astype(np.float32)
+            ssum = np.float32(e.sum(dtype=np.float64))
+            p = round_dt(round_dt(e, dt) * (np.float32(1.0) / ssum), dt)
+            out[s, h * D:(h + 1) * D] = round_dt((p.astype(np.float64) @ v[hk, :L].astype(np.float64)).astype(np.float32),
+                                                 dt)
+    return out

@@ -41,7 +41,7 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, outq):
     import torch
     import torch.distributed as dist
     sys.path.insert(0, str(ROOT))
@@ -98,26 +98,27 @@ def _worker(rank, world, port, q):
                 a, b = from_dev(tp), from_dev(single)
                 res[name + "_steps"] = float((np.abs(a - b) / (ulp(b, "bf16") + 1e-6)).max())
             res["tok_tp"], res["tok_single"] = int(step.tok.item()), int(tok.item())
-        q.put((rank, res))
+        outq.put((rank, res))
+        dist.barrier()
         comm.close()
         dist.destroy_process_group()
     except Exception as e:  # noqa: BLE001
-        q.put((rank, {"ok": False, "error": repr(e)}))
+        outq.put((rank, {"ok": False, "error": repr(e)}))
 
 
 @pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
 def test_tp2_decode_step_matches_single_gpu():
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
-    q = ctx.Queue()
+    outq = ctx.Queue()
     port = _port()
     env_nvls = os.environ.get("NCCL_NVLS_ENABLE")
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, outq)) for r in range(2)]
     try:
         for p in procs:
             p.start()
-        results = dict(q.get(timeout=300) for _ in procs)
+        results = dict(outq.get(timeout=300) for _ in procs)
         for p in procs:
             p.join(timeout=120)
     finally:
