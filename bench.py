@@ -220,7 +220,7 @@ class TPStep:
     def __init__(self, torch, dev, seed, world, rank):
         import infengine_b200 as ie
         from infengine_b200.host import rope_tables
-        from infengine_b200.tp import Comm, ShardPlan, TPDecodeStep
+        from infengine_b200.tp import Comm, P2PExchange, ShardPlan, TPDecodeStep
         self.ie, self.torch = ie, torch
         self.plan = ShardPlan(world, rank)
         g = torch.Generator(device=dev)
@@ -239,8 +239,12 @@ class TPStep:
         torch.cuda.empty_cache()
         cos, sin = rope_tables(CTX)
         self.comm = Comm(world, rank)
+        # O and down: one fused GEMV + NVLink exchange kernel each (default), or
+        # fp32 partial + NCCL allreduce + cast (IE_TP_EXCHANGE=nccl)
+        self.mode = os.environ.get("IE_TP_EXCHANGE", "p2p")
+        self.exchange = P2PExchange(world, rank) if self.mode == "p2p" else None
         self.inner = TPDecodeStep(self.plan, self.comm, layers, lm, torch.from_numpy(cos).to(dev),
-                                  torch.from_numpy(sin).to(dev), POS)
+                                  torch.from_numpy(sin).to(dev), POS, exchange=self.exchange)
         g2 = torch.Generator(device=dev)
         g2.manual_seed(seed + 1)
         self.inner.x.copy_(torch.randn(1, H, generator=g2, device=dev, dtype=torch.float32).to(torch.bfloat16))
@@ -257,6 +261,8 @@ class TPStep:
             self.ie.ffn_gate_up(self.x, w["wg"], w["wu"], self.h)
 
     def close(self):
+        if self.exchange is not None:
+            self.exchange.close()
         self.comm.close()
 
 
@@ -533,6 +539,7 @@ def main():
             "weight_bytes_per_step": WEIGHT_BYTES,
             "l2": "inputs larger than L2 (15.01 GB of weights streamed per step)",
             "parallelism": f"tp{world}" if world > 1 else "single",
+            "tp_exchange": getattr(step, "mode", None),
             "launch": "one CUDA graph per step" if args.impl == "ours" else "eager, legacy default stream",
         },
         "matmul_hbm_gbs": round(WEIGHT_BYTES / (ms_step / 1e3) / 1e9, 1),

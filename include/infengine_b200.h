@@ -230,6 +230,33 @@ int ie_argmax_allreduce(ie_comm* comm, unsigned long long* keys, int M, int* idx
 /* out[i] = round_dt(in[i]) for n values. */
 int ie_cast_f32(ie_dtype dt, const float* in, void* out, size_t n, void* stream);
 
+/* Row-split projection fused with its allreduce (decode, M <= 16): every
+ * rank runs this on its column shard of X and W; each CTA pushes its fp32
+ * partial rows, every value tagged with the call's epoch in one 64-bit word,
+ * into every rank's exchange buffer over NVLink as soon as they are computed;
+ * the CTA that completes a rank's grid waits (bounded; IE_ERR_TIMEOUT in
+ * ie_device_status) until every rank's words of this call have arrived and
+ * writes
+ *   Y[M,N] = round_dt(sum over ranks, in rank order, of the partials).
+ * One kernel per projection replaces ie_gemm_f32out + ie_allreduce_sum_f32 +
+ * ie_cast_f32. All ranks must make the same sequence of calls.
+ * The exchange: one device buffer per rank of ie_tp_exchange_bytes(world,
+ * max_rows, max_cols) bytes, zeroed once, exported with ie_ipc_export and
+ * mapped by every other rank with ie_ipc_import; sym is a DEVICE array of
+ * world pointers (this process's mapping of every rank's buffer). */
+typedef struct ie_tp_exchange {
+  int world, rank;
+  void* const* sym;
+  int max_rows, max_cols;
+} ie_tp_exchange;
+size_t ie_tp_exchange_bytes(int world, int max_rows, int max_cols);
+int ie_ipc_export(const void* dev_ptr, void* handle_out_64_bytes, uint64_t* offset_out);
+int ie_ipc_import(const void* handle_64_bytes, uint64_t offset, void** dev_ptr_out);
+int ie_ipc_release(void* dev_ptr);
+int ie_gemm_allreduce(ie_dtype dt, int M, int N, int K,
+                      const void* X, int64_t ldx, const void* W, int64_t ldw,
+                      void* Y, int64_t ldy, const ie_tp_exchange* ex, void* stream);
+
 /* Global vocabulary id held in a packed argmax key. */
 static inline int ie_argmax_key_index(unsigned long long key) {
   unsigned int tie = ~(unsigned int)(key & 0xffffffffull);

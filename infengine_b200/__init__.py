@@ -53,7 +53,9 @@ STATUS = {
 EXPORTED_SYMBOLS = (
     "ie_status_string", "ie_version", "ie_gemm", "ie_swiglu", "ie_ffn_workspace_size", "ie_ffn", "ie_ffn_gate_up",
     "ie_qkv", "ie_lm_head_argmax_workspace_size", "ie_lm_head_argmax", "ie_argmax", "ie_device_status",
-    "ie_lm_head_argmax_noalloc", "ie_attention",
+    "ie_lm_head_argmax_noalloc", "ie_attention", "ie_gemm_f32out", "ie_comm_unique_id", "ie_comm_create",
+    "ie_comm_destroy", "ie_allreduce_sum_f32", "ie_argmax_allreduce", "ie_cast_f32", "ie_tp_exchange_bytes",
+    "ie_ipc_export", "ie_ipc_import", "ie_ipc_release", "ie_gemm_allreduce",
 )
 
 

@@ -54,7 +54,9 @@ const char* ie_version(void) { return "0.1.0"; }
 
 int ie_device_status(int clear) {
   if (cudaDeviceSynchronize() != cudaSuccess) return IE_ERR_LAUNCH;
-  return read_tc_status(clear != 0);
+  const int a = read_tc_status(clear != 0);
+  const int b = read_tp_status(clear != 0);
+  return a != IE_OK ? a : b;
 }
 
 int ie_gemm(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, void* Y,

@@ -100,13 +100,83 @@ __device__ __forceinline__ const T* weight_row(const SkinnyParams& p, int tile, 
   }
 }
 
+// Device status word of the tensor-parallel exchange (IE_ERR_TIMEOUT when a
+// bounded wait for another rank's rows gave up).
+__device__ int g_tp_status = 0;
+
 // Epilogues, run by warp 0 on the fully reduced tile.
 // acc[.][mt][i]: weight row g + 8*(i>>1) of the tile, batch row m = mt*8 + 2t + (i&1).
 template <typename T, int MT, int EPI>
 __device__ __forceinline__ void epilogue(const SkinnyParams& p, int tile, int g, int t, int lane,
                                          const bool (&rvalid)[2], const int (&nidx)[2],
                                          float (&acc)[EpiTraits<EPI>::nmat][MT][4]) {
-  if constexpr (EPI == EPI_STORE_F32) {
+  if constexpr (EPI == EPI_TP_ALLREDUCE) {
+    // Each partial value travels with the call's epoch in one 64-bit word
+    // (single-copy atomic), pushed straight into this rank's slot of every
+    // rank's inbox (NVLink stores for peers). The CTA then reads back, from
+    // its own inbox, the same tile rows of every rank (waiting, bounded, for
+    // words still carrying an older epoch) and writes their rank-ordered sum.
+    // A value has arrived exactly when its epoch matches: no fence, no flag.
+    // Every rank's CTA j waits only for the other ranks' CTA j, so the whole
+    // grid must be resident (checked at launch).
+    const unsigned int e =
+        *reinterpret_cast<const volatile unsigned int*>(&static_cast<const TpHeader*>(p.tp_sym[p.tp_rank])->epoch) + 1u;
+    const int parity = (int)(e & 1u);
+    const size_t slot = (size_t)p.tp_rows * p.tp_cols;
+    const size_t base = (size_t)parity * p.tp_world * slot;
+    for (int peer = 0; peer < p.tp_world; ++peer) {
+      unsigned long long* box = reinterpret_cast<unsigned long long*>(static_cast<char*>(p.tp_sym[peer]) +
+                                                                       kTpInboxOffset) +
+                                base + (size_t)p.tp_rank * slot;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = i >> 1, m = mt * 8 + 2 * t + (i & 1);
+          if (rvalid[r] && m < p.M) {
+            const unsigned long long word =
+                ((unsigned long long)e << 32) | (unsigned long long)__float_as_uint(acc[0][mt][i]);
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(box + (size_t)m * p.tp_cols + nidx[r]),
+                         "l"(word)
+                         : "memory");
+          }
+        }
+    }
+    const unsigned long long* inbox = reinterpret_cast<const unsigned long long*>(
+                                          static_cast<const char*>(p.tp_sym[p.tp_rank]) + kTpInboxOffset) +
+                                      base;
+    T* Y = static_cast<T*>(p.Y);
+    unsigned long long t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    bool gave_up = false;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = i >> 1, m = mt * 8 + 2 * t + (i & 1);
+        if (!rvalid[r] || m >= p.M || gave_up) continue;
+        float sum = 0.f;
+        for (int q = 0; q < p.tp_world && !gave_up; ++q) {
+          const unsigned long long* w = inbox + (size_t)q * slot + (size_t)m * p.tp_cols + nidx[r];
+          while (true) {
+            unsigned long long v;
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(w) : "memory");
+            if ((unsigned int)(v >> 32) == e) {
+              sum += __uint_as_float((unsigned int)(v & 0xffffffffull));
+              break;
+            }
+            unsigned long long now;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+            if (now - t0 > 2000000000ull) {
+              atomicExch(&g_tp_status, IE_ERR_TIMEOUT);
+              gave_up = true;
+              break;
+            }
+          }
+        }
+        if (!gave_up) Y[(int64_t)m * p.ldy + nidx[r]] = DT<T>::from_f(sum);
+      }
+  } else if constexpr (EPI == EPI_STORE_F32) {
     float* Y = static_cast<float*>(p.Y);
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
@@ -207,6 +277,26 @@ __device__ __forceinline__ void epilogue(const SkinnyParams& p, int tile, int g,
         dst[d] = DT<T>::from_f(a);
         dst[d + 64] = DT<T>::from_f(b);
       }
+  }
+}
+
+// Call bookkeeping of EPI_TP_ALLREDUCE: the CTA that completes the grid
+// (every CTA has read this call's epoch and finished its rows by then)
+// advances the epoch and re-arms the completion counter for the next call.
+// The inbox slots alternate with the call parity, so a fast rank's next call
+// never overwrites words a slow rank has not read yet: a rank finishes call
+// e+1 only after every rank wrote its call-e+1 words, which each rank does
+// only after finishing call e.
+template <typename T>
+__device__ void tp_finish(const SkinnyParams& p) {
+  TpHeader* own = static_cast<TpHeader*>(p.tp_sym[p.tp_rank]);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&own->done, 1u) == (unsigned)p.tiles - 1u) {
+      own->done = 0u;
+      *reinterpret_cast<volatile unsigned int*>(&own->epoch) += 1u;
+    }
   }
 }
 
@@ -376,6 +466,7 @@ __global__ void __launch_bounds__(kThreads) skinny_kernel(const SkinnyParams p) 
           }
       epilogue<T, MT, EPI>(p, tile, g, t, lane, rvalid, nidx, acc);
     }
+    if constexpr (EPI == EPI_TP_ALLREDUCE) tp_finish<T>(p);
 #if IE_SK_PERSIST
     __syncthreads();  // red is reused by the next tile
 #endif
@@ -520,6 +611,11 @@ template <typename T, int MT, int EPI>
 static cudaError_t launch_variant(const SkinnyParams& p, cudaStream_t st) {
   auto kernel = skinny_kernel<T, MT, EPI>;
   int grid = p.tiles;
+  if constexpr (EPI == EPI_TP_ALLREDUCE) {
+    // every CTA waits for the same tile of the other ranks: all must fit at once
+    static const int resident = resident_ctas(kernel);
+    if (grid > resident) return cudaErrorCooperativeLaunchTooLarge;
+  }
 #if IE_SK_PERSIST
   static const int resident = resident_ctas(kernel);
   grid = p.tiles < resident ? p.tiles : resident;
@@ -551,11 +647,22 @@ cudaError_t launch_skinny(ie_dtype dt, int epi, const SkinnyParams& p, cudaStrea
     case EPI_ARGMAX: return launch_skinny_t<T, EPI_ARGMAX>(p, tiles, st); \
     case EPI_QKV: return launch_skinny_t<T, EPI_QKV>(p, tiles, st);      \
     case EPI_STORE_F32: return launch_skinny_t<T, EPI_STORE_F32>(p, tiles, st); \
+    case EPI_TP_ALLREDUCE: return launch_skinny_t<T, EPI_TP_ALLREDUCE>(p, tiles, st); \
   }
   if (dt == IE_DTYPE_F16) { IE_SK(__half) }
   else { IE_SK(__nv_bfloat16) }
 #undef IE_SK
   return cudaErrorInvalidValue;
+}
+
+int read_tp_status(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_tp_status, sizeof(int)) != cudaSuccess) return IE_ERR_LAUNCH;
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_tp_status, &z, sizeof(int));
+  }
+  return v;
 }
 
 cudaError_t launch_swiglu(ie_dtype dt, int64_t n, const void* gate, const void* up, void* out, cudaStream_t st) {

@@ -12,7 +12,20 @@ enum SkinnyEpilogue {
   EPI_ARGMAX = 2,  // logits (optional store) + packed-key argmax per batch row
   EPI_QKV = 3,     // head-major scatter of Q / K-cache / V-cache rows, optional RoPE
   EPI_STORE_F32 = 4,  // Y (float) [m, n] = acc, unrounded (tensor-parallel partial sums)
+  EPI_TP_ALLREDUCE = 5,  // partial rows pushed to every rank's inbox over NVLink; the last CTA
+                         // sums all ranks' partials (rank order) into Y (dt)
 };
+
+// Layout of one rank's exchange buffer (ie_gemm_allreduce): a 256-byte
+// header (call counter, CTA completion counter), then 2 x world inbox slots of
+// tp_rows x tp_cols 64-bit words (fp32 value | call epoch << 32),
+// double-buffered by call parity.
+struct TpHeader {
+  unsigned int epoch;
+  unsigned int done;
+};
+constexpr size_t kTpInboxOffset = 1024;
+constexpr int kTpMaxWorld = 8;
 
 struct SkinnyParams {
   const void* X = nullptr;
@@ -43,10 +56,16 @@ struct SkinnyParams {
   int pos0 = 0;
   const float* rope_cos = nullptr;
   const float* rope_sin = nullptr;
+  // EPI_TP_ALLREDUCE: device array [tp_world] of every rank's symmetric
+  // buffer as mapped in this process (own buffer at tp_rank)
+  void* const* tp_sym = nullptr;
+  int tp_world = 0, tp_rank = 0, tp_rows = 0, tp_cols = 0;
 };
 
 cudaError_t launch_skinny(ie_dtype dt, int epi, const SkinnyParams& p, cudaStream_t st);
 cudaError_t launch_swiglu(ie_dtype dt, int64_t n, const void* gate, const void* up, void* out, cudaStream_t st);
+// Device status word of the tensor-parallel exchange (IE_OK or IE_ERR_TIMEOUT).
+int read_tp_status(bool clear);
 cudaError_t launch_argmax(ie_dtype dt, int M, int V, const void* logits, int64_t ld, int* idx_out, cudaStream_t st);
 
 }  // namespace ie

@@ -134,6 +134,64 @@ class Comm:
             self.handle = ctypes.c_void_p()
 
 
+class _Exchange(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int), ("sym", ctypes.c_void_p),
+                ("max_rows", ctypes.c_int), ("max_cols", ctypes.c_int)]
+
+
+class P2PExchange:
+    """Exchange buffers for ie_gemm_allreduce: one zeroed device buffer per
+    rank, mapped into every other rank with CUDA IPC (handles distributed over
+    the torch.distributed group). All ranks construct it together."""
+
+    def __init__(self, world: int, rank: int, max_rows: int = 16, max_cols: int = HIDDEN_SIZE, group=None):
+        import torch
+        import torch.distributed as dist
+        L = lib()
+        L.ie_tp_exchange_bytes.restype = ctypes.c_size_t
+        L.ie_tp_exchange_bytes.argtypes = [ctypes.c_int] * 3
+        L.ie_ipc_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)]
+        L.ie_ipc_import.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]
+        L.ie_ipc_release.argtypes = [ctypes.c_void_p]
+        L.ie_gemm_allreduce.argtypes = [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_int64] * 3 + [
+            ctypes.POINTER(_Exchange), ctypes.c_void_p]
+        nbytes = int(L.ie_tp_exchange_bytes(world, max_rows, max_cols))
+        self.buf = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+        torch.cuda.synchronize()
+        handle = (ctypes.c_ubyte * 64)()
+        off = ctypes.c_uint64()
+        _check(L.ie_ipc_export(ctypes.c_void_p(self.buf.data_ptr()), ctypes.cast(handle, ctypes.c_void_p),
+                               ctypes.byref(off)), "ie_ipc_export")
+        everyone = [None] * world
+        dist.all_gather_object(everyone, (bytes(handle), int(off.value)), group=group)
+        self.imported = []
+        ptrs = []
+        for r, (h, o) in enumerate(everyone):
+            if r == rank:
+                ptrs.append(self.buf.data_ptr())
+                continue
+            hb = (ctypes.c_ubyte * 64).from_buffer_copy(h)
+            p = ctypes.c_void_p()
+            _check(L.ie_ipc_import(ctypes.cast(hb, ctypes.c_void_p), o, ctypes.byref(p)), "ie_ipc_import")
+            self.imported.append(p)
+            ptrs.append(p.value)
+        self.sym = torch.tensor(ptrs, dtype=torch.int64, device="cuda")
+        self.desc = _Exchange(world, rank, ctypes.c_void_p(self.sym.data_ptr()), max_rows, max_cols)
+        dist.barrier(group=group)
+
+    def gemm_allreduce(self, x, w, y, stream=None):
+        """y[M,N] = round(sum over ranks of x_r . w_r^T), one fused kernel."""
+        M, K = x.shape
+        N = w.shape[0]
+        _check(lib().ie_gemm_allreduce(_dt(x), M, N, K, _ptr(x), x.stride(0), _ptr(w), w.stride(0), _ptr(y),
+                                       y.stride(0), ctypes.byref(self.desc), _stream(stream)), "ie_gemm_allreduce")
+
+    def close(self):
+        for p in self.imported:
+            lib().ie_ipc_release(p)
+        self.imported = []
+
+
 def cast_f32(src, dst, stream=None):
     _check(lib().ie_cast_f32(_dt(dst), _ptr(src), _ptr(dst), src.numel(), _stream(stream)), "ie_cast_f32")
 
@@ -160,10 +218,11 @@ class TPDecodeStep:
     """
 
     def __init__(self, plan: ShardPlan, comm: Comm, layers: list, lm_shard, rope_cos, rope_sin, pos: int,
-                 batch: int = 1, ctx: int = 8192):
+                 batch: int = 1, ctx: int = 8192, exchange: "P2PExchange | None" = None):
         import torch
         from . import lm_head_workspace_bytes
         self.plan, self.comm, self.layers, self.lm = plan, comm, layers, lm_shard
+        self.exchange = exchange
         self.cos, self.sin, self.pos, self.ctx = rope_cos, rope_sin, pos, ctx
         dev, dt = lm_shard.device, lm_shard.dtype
         M, H = batch, plan.hidden
@@ -178,7 +237,8 @@ class TPDecodeStep:
         self.keys = torch.zeros(M, device=dev, dtype=torch.int64)
         self.tok = torch.zeros(M, device=dev, dtype=torch.int32)
         self.ws = torch.zeros(lm_head_workspace_bytes(M), dtype=torch.uint8, device=dev)
-        self.launches_per_step = len(layers) * 8 + 2  # kernels of this library (NCCL kernels not counted)
+        # kernels of this library per step (NCCL's own kernels not counted)
+        self.launches_per_step = len(layers) * (4 if exchange else 8) + 2
 
     def __call__(self):
         from . import ffn_gate_up, lm_head_argmax, qkv
@@ -186,7 +246,14 @@ class TPDecodeStep:
         for l, w in enumerate(self.layers):
             qkv(self.x, w["wq"], w["wk"], w["wv"], self.q, self.kc[l], self.vc[l], self.ctx * p.head_dim, self.pos,
                 self.cos, self.sin, n_q_heads=p.q_heads, n_kv_heads=p.kv_heads)
-            gemm_f32out(self.q.view(M, -1) if M == 1 else self.q.permute(1, 0, 2).reshape(M, -1), w["wo"], self.part)
+            a_in = self.q.view(M, -1) if M == 1 else self.q.permute(1, 0, 2).reshape(M, -1)
+            if self.exchange is not None:
+                # one kernel: partial O rows to every rank over NVLink, summed on arrival
+                self.exchange.gemm_allreduce(a_in, w["wo"], self.attn_out)
+                ffn_gate_up(self.x, w["wg"], w["wu"], self.h)
+                self.exchange.gemm_allreduce(self.h, w["wd"], self.ffn_out)
+                continue
+            gemm_f32out(a_in, w["wo"], self.part)
             self.comm.allreduce_sum_f32(self.part)
             cast_f32(self.part, self.attn_out)
             ffn_gate_up(self.x, w["wg"], w["wu"], self.h)

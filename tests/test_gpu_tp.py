@@ -41,14 +41,14 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, outq):
+def _worker(rank, world, port, outq, mode):
     import torch
     import torch.distributed as dist
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(ROOT / "tests"))
     import infengine_b200 as ie
     from infengine_b200.host import rope_tables
-    from infengine_b200.tp import Comm, ShardPlan, TPDecodeStep
+    from infengine_b200.tp import Comm, P2PExchange, ShardPlan, TPDecodeStep
     from conftest import from_dev, ulp
     try:
         torch.cuda.set_device(rank)
@@ -69,10 +69,12 @@ def _worker(rank, world, port, outq):
         cos, sin = (torch.from_numpy(t).to(dev) for t in rope_tables(CTX))
         plan = ShardPlan(world, rank)
         comm = Comm(world, rank)
+        exchange = P2PExchange(world, rank) if mode == "p2p" else None
         step = TPDecodeStep(plan, comm, [plan.shard_layer(f) for f in fulls], plan.shard_lm_head(lm), cos, sin, POS,
-                            ctx=CTX)
+                            ctx=CTX, exchange=exchange)
         step.x.copy_(x)
-        step()
+        for _ in range(3):  # repeated calls exercise both exchange parities
+            step()
         torch.cuda.synchronize()
         res = {"ok": True}
         if rank == 0:
@@ -98,8 +100,11 @@ def _worker(rank, world, port, outq):
                 a, b = from_dev(tp), from_dev(single)
                 res[name + "_steps"] = float((np.abs(a - b) / (ulp(b, "bf16") + 1e-6)).max())
             res["tok_tp"], res["tok_single"] = int(step.tok.item()), int(tok.item())
+        res["status"] = ie.device_status()
         outq.put((rank, res))
         dist.barrier()
+        if exchange is not None:
+            exchange.close()
         comm.close()
         dist.destroy_process_group()
     except Exception as e:  # noqa: BLE001
@@ -107,14 +112,15 @@ def _worker(rank, world, port, outq):
 
 
 @pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
-def test_tp2_decode_step_matches_single_gpu():
+@pytest.mark.parametrize("mode", ["p2p", "nccl"])
+def test_tp2_decode_step_matches_single_gpu(mode):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     outq = ctx.Queue()
     port = _port()
     env_nvls = os.environ.get("NCCL_NVLS_ENABLE")
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, outq)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, outq, mode)) for r in range(2)]
     try:
         for p in procs:
             p.start()
@@ -134,3 +140,4 @@ def test_tp2_decode_step_matches_single_gpu():
     assert r0["q_equal"] and r0["k_equal"], r0
     assert r0["attn_steps"] <= 1.0 and r0["down_steps"] <= 1.0, r0
     assert r0["tok_tp"] == r0["tok_single"], r0
+    assert all(r["status"] == 0 for r in results.values()), results
