@@ -260,6 +260,22 @@ class TPStep:
         for w in self.layers:
             self.ie.ffn_gate_up(self.x, w["wg"], w["wu"], self.h)
 
+    def setup_prefill(self, S: int):
+        """M=S prefill over the same shards (tensor-core kernels, NCCL allreduce)."""
+        from infengine_b200.tp import TPDecodeStep
+        inner = self.inner
+        self.pre = TPDecodeStep(self.plan, self.comm, self.layers, self.inner.lm, inner.cos, inner.sin, 0,
+                                batch=S, ctx=CTX, exchange=None, lm_rows=1)
+        g = self.torch.Generator(device=inner.x.device)
+        g.manual_seed(7)
+        self.pre.x.copy_(self.torch.randn(S, H, generator=g, device=inner.x.device).to(self.torch.bfloat16))
+
+    def prefill(self):
+        self.pre()
+
+    def prefill_flops(self):
+        return self.pre.flops()
+
     def close(self):
         if self.exchange is not None:
             self.exchange.close()
@@ -303,6 +319,81 @@ class RefStep:
             R.ref_ffn(1, p(self.x), p(self.ffn_out), p(w["wu"]), p(w["wd"]), p(w["wg"]), p(self.ws))
         R.ref_lm_head(1, p(self.x), p(self.lm), p(self.logits))
         R.ref_sample_token_amax(p(self.logits), p(self.tok))
+
+
+# ------------------------------------------------- per-config measurements
+def per_config(torch, step, stream, hbm_peak, tf_peak):
+    """BASELINE configs 1-4 one by one on the already-resident model weights
+    (each timed over all 32 layers' copies, or 4 lm_head launches, so the
+    weights stream from HBM, not L2): GB/s for the HBM-bound decode shapes,
+    TFLOP/s for the prefill GEMMs."""
+    import infengine_b200 as ie
+    dev, bf = step.x.device, torch.bfloat16
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn, reps=5):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            fn()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+        with torch.cuda.stream(stream):
+            g.replay()
+            ev0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+        t = ev0.elapsed_time(ev1) / 1e3 / reps
+        g.reset()
+        return t
+
+    out = {}
+    Ls = step.layers
+    # config 1: y[1,4096] = x . W[4096,4096]^T (the O weights of the 32 layers)
+    x1, y1 = step.x[:1], torch.empty(1, H, device=dev, dtype=bf)
+    t = timed(lambda: [ie.gemm(x1, w["wo"], y1) for w in Ls]) / L
+    b = 2 * (H * H + 2 * H)
+    out["c1_gemv_4096x4096"] = {"us": round(t * 1e6, 2), "gbs": round(b / t / 1e9, 1),
+                                "frac_hbm": round(b / t / 1e9 / hbm_peak, 4)}
+    # config 2: FFN block at M in {1,4,8}
+    c2 = {}
+    for m in (1, 4, 8):
+        xm = torch.randn(m, H, device=dev).to(bf)
+        om = torch.empty(m, H, device=dev, dtype=bf)
+        ws = torch.empty(ie.ffn_workspace_bytes(m, F), dtype=torch.uint8, device=dev)
+        t = timed(lambda: [ie.ffn_fused(xm, w["wu"], w["wd"], w["wg"], om, ws) for w in Ls]) / L
+        b = 2 * (3 * F * H + 2 * m * H)
+        c2[f"m{m}"] = {"us": round(t * 1e6, 2), "gbs": round(b / t / 1e9, 1), "frac_hbm": round(b / t / 1e9 / hbm_peak, 4)}
+    out["c2_ffn_decode"] = c2
+    # config 4: lm_head + argmax at B in {1,8,64}
+    c4 = {}
+    for B in (1, 8, 64):
+        xb = torch.randn(B, H, device=dev).to(bf)
+        wsb = torch.zeros(ie.lm_head_workspace_bytes(B), dtype=torch.uint8, device=dev)
+        ib = torch.zeros(B, dtype=torch.int32, device=dev)
+        t = timed(lambda: [ie.lm_head_argmax(xb, step.lm, wsb, idx_out=ib) for _ in range(4)]) / 4
+        b = 2 * (V * H + B * H)
+        c4[f"b{B}"] = {"us": round(t * 1e6, 2), "gbs": round(b / t / 1e9, 1), "frac_hbm": round(b / t / 1e9 / hbm_peak, 4),
+                       "tflops": round(2 * B * V * H / t / 1e12, 2)}
+    out["c4_lm_head_argmax"] = c4
+    # config 3: each prefill projection at M=2048 over the 32 layers
+    S = step.S
+    c3 = {}
+    for name, fn, flops in (
+        ("qkv_6144x4096", lambda: [ie.qkv(step.xp, w["wq"], w["wk"], w["wv"], step.qp, step.kc[l], step.vc[l], CTX * HD,
+                                          0, step.cos, step.sin) for l, w in enumerate(Ls)], 2 * S * 6144 * H),
+        ("o_4096x4096", lambda: [ie.gemm(step.qp.view(S, H), w["wo"], step.ap) for w in Ls], 2 * S * H * H),
+        ("gate_up_2x14336x4096", lambda: [ie.ffn_gate_up(step.xp, w["wg"], w["wu"], step.hp) for w in Ls],
+         2 * S * 2 * F * H),
+        ("down_4096x14336", lambda: [ie.gemm(step.hp, w["wd"], step.op) for w in Ls], 2 * S * H * F),
+    ):
+        t = timed(fn, reps=2) / L
+        c3[name] = {"us": round(t * 1e6, 1), "tflops": round(flops / t / 1e12, 1),
+                    "frac_burst": round(flops / t / 1e12 / tf_peak, 4)}
+    out["c3_prefill_m2048"] = c3
+    return out
 
 
 # -------------------------------------------------------------- CPU baseline
@@ -576,6 +667,34 @@ def main():
             "avg_launch_us": round(per_launch_s * 1e6, 2),
         }
         result["step_roofline_frac"] = round(WEIGHT_BYTES / world / (ms_step / 1e3) / 1e9 / hbm_peak, 4)
+    if args.impl == "ours" and world > 1:
+        # BASELINE config 3 under tensor parallelism: M=2048 projection chain,
+        # per-rank shards on the tensor-core kernels, NCCL allreduce of the
+        # fp32 O / down partials (32 MB each); aggregate TFLOP/s over ranks
+        step.setup_prefill(2048)
+        gp = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            step.prefill()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(gp, stream=stream):
+            step.prefill()
+        with torch.cuda.stream(stream):
+            gp.replay()
+            ev0.record(stream)
+            for _ in range(3):
+                gp.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([ev0.elapsed_time(ev1) / 1e3 / 3], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pre_s = float(t.item())
+        tflops = step.prefill_flops() * world / pre_s / 1e12
+        result["prefill"] = {"workload": f"M=2048 tokens, tp{world}: 32 x [QKV+RoPE, O+allreduce, gate/up+SwiGLU, "
+                                         f"down+allreduce] + lm_head(last row)", "ms": round(pre_s * 1e3, 3),
+                             "tflops_aggregate": round(tflops, 1),
+                             "frac_of_n_x_sustained": round(tflops / (world * tf_peak_sus), 4)}
+        gp.reset()
+        del gp
     if args.impl == "ours" and world == 1:
         # prefill projection GEMMs at M=2048 over all 32 layers
         step.setup_prefill(2048)
@@ -603,6 +722,7 @@ def main():
             "gpu_launches": 4 * L,
         }
         del gp
+        result["configs"] = per_config(torch, step, stream, hbm_peak, tf_peak)
         # BASELINE config 5 shapes of the same path: batch-8 decode and the M=5
         # verify pass (4 draft tokens + 1), same weights, one graph per step
         for name, m in (("decode_bs8", 8), ("verify_m5", 5)):

@@ -58,7 +58,9 @@ const char* ie_version(void);
 /* Device-side status of the current device: IE_OK, or IE_ERR_TIMEOUT when a
  * bounded wait inside a tensor-core kernel gave up (the kernel then drained
  * its own copies, freed its tensor memory and returned without finishing).
- * Synchronizes the device. clear != 0 resets the word to IE_OK. */
+ * IE_ERR_INVALID_ARG when a batched QKV row carried a position outside its
+ * cache (the row was skipped). Synchronizes the device. clear != 0 resets the
+ * words to IE_OK. */
 int ie_device_status(int clear);
 
 /* ---- a1 / a5: projection GEMM --------------------------------------------
@@ -136,6 +138,20 @@ int ie_qkv(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_di
            int64_t cache_head_stride, int pos0,
            const float* rope_cos, const float* rope_sin,
            void* stream);
+
+/* Batched decode of B independent sequences (BASELINE config 5 at batch 8):
+ * row b of x is a token of sequence b at position positions[b] (device array
+ * [B]); its K/V rows go to sequence b's cache, which starts cache_batch_stride
+ * elements after sequence b-1's ([B][n_kv_heads][cache_rows][128] with the
+ * usual head stride). Q is written [n_q_heads][B][128]. A position outside
+ * [0, cache_rows) leaves that row unwritten and sets IE_ERR_INVALID_ARG in
+ * ie_device_status. No counterpart in the reference (batch 1 only). */
+int ie_qkv_batched(ie_dtype dt, int B, int H, int n_q_heads, int n_kv_heads, int head_dim,
+                   const void* x, const void* Wq, const void* Wk, const void* Wv,
+                   void* q_out, void* k_cache, void* v_cache,
+                   int64_t cache_head_stride, int64_t cache_batch_stride, int cache_rows,
+                   const int* positions, const float* rope_cos, const float* rope_sin,
+                   void* stream);
 
 /* ---- attention core behind the drop-in attn / decode_attn ---------------
  * Replaces the score / softmax / value steps of attn and decode_attn

@@ -55,7 +55,7 @@ EXPORTED_SYMBOLS = (
     "ie_qkv", "ie_lm_head_argmax_workspace_size", "ie_lm_head_argmax", "ie_argmax", "ie_device_status",
     "ie_lm_head_argmax_noalloc", "ie_attention", "ie_gemm_f32out", "ie_comm_unique_id", "ie_comm_create",
     "ie_comm_destroy", "ie_allreduce_sum_f32", "ie_argmax_allreduce", "ie_cast_f32", "ie_tp_exchange_bytes",
-    "ie_ipc_export", "ie_ipc_import", "ie_ipc_release", "ie_gemm_allreduce",
+    "ie_ipc_export", "ie_ipc_import", "ie_ipc_release", "ie_gemm_allreduce", "ie_qkv_batched",
 )
 
 
@@ -89,6 +89,9 @@ def lib() -> ctypes.CDLL:
         L.ie_ffn_gate_up.argtypes = [i32, i32, i32, i32, vp, vp, vp, vp, i64, vp]
         L.ie_ffn_gate_up.restype = i32
         L.ie_qkv.argtypes = [i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, i64, i32, vp, vp, vp]
+        L.ie_qkv_batched.argtypes = [i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, i64, i64, i32, vp, vp,
+                                     vp, vp]
+        L.ie_qkv_batched.restype = i32
         L.ie_lm_head_argmax_workspace_size.restype = sz
         L.ie_lm_head_argmax_workspace_size.argtypes = [i32]
         L.ie_lm_head_argmax.argtypes = [i32, i32, i32, i32, i64, vp, i64, vp, vp, i64, vp, vp, vp, sz, vp]
@@ -184,6 +187,17 @@ def attention(q, k_cache, v_cache, out, pos0, n_kv_heads=NUM_KV_HEADS, stream=No
     nq, S, D = q.shape
     _check(lib().ie_attention(_dt(q), S, pos0, nq, n_kv_heads, D, _ptr(q), q.stride(0), _ptr(k_cache), _ptr(v_cache),
                               k_cache.stride(0), _ptr(out), out.stride(0), _stream(stream)), "ie_attention")
+
+
+def qkv_batched(x, wq, wk, wv, q_out, k_cache, v_cache, positions, rope_cos=None, rope_sin=None,
+                n_q_heads=NUM_Q_HEADS, n_kv_heads=NUM_KV_HEADS, head_dim=HEAD_DIM, stream=None):
+    """ie_qkv_batched: row b of x is sequence b's token at positions[b];
+    caches are [B, n_kv_heads, rows, 128]."""
+    B, H = x.shape
+    _check(lib().ie_qkv_batched(_dt(x), B, H, n_q_heads, n_kv_heads, head_dim, _ptr(x), _ptr(wq), _ptr(wk), _ptr(wv),
+                                _ptr(q_out), _ptr(k_cache), _ptr(v_cache), k_cache.stride(1), k_cache.stride(0),
+                                k_cache.shape[2], _ptr(positions), _ptr(rope_cos), _ptr(rope_sin), _stream(stream)),
+           "ie_qkv_batched")
 
 
 def lm_head_workspace_bytes(M: int) -> int:

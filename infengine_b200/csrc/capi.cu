@@ -55,7 +55,7 @@ const char* ie_version(void) { return "0.1.0"; }
 int ie_device_status(int clear) {
   if (cudaDeviceSynchronize() != cudaSuccess) return IE_ERR_LAUNCH;
   const int a = read_tc_status(clear != 0);
-  const int b = read_tp_status(clear != 0);
+  const int b = read_skinny_status(clear != 0);
   return a != IE_OK ? a : b;
 }
 
@@ -151,9 +151,12 @@ int ie_ffn_gate_up(ie_dtype dt, int M, int H, int F, const void* x, const void* 
   return launch_tc_gemm(dt, q, st);
 }
 
-int ie_qkv(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_dim, const void* x, const void* Wq,
-           const void* Wk, const void* Wv, void* q_out, void* k_cache, void* v_cache, int64_t cache_head_stride,
-           int pos0, const float* rope_cos, const float* rope_sin, void* stream) {
+namespace {
+
+int qkv_common(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_dim, const void* x, const void* Wq,
+               const void* Wk, const void* Wv, void* q_out, void* k_cache, void* v_cache, int64_t cache_head_stride,
+               int pos0, const int* positions, int64_t cache_batch_stride, int cache_rows, const float* rope_cos,
+               const float* rope_sin, void* stream) {
   if (!valid_dtype(dt) || M < 0 || H <= 0 || n_q_heads <= 0 || n_kv_heads < 0 || pos0 < 0) return IE_ERR_INVALID_ARG;
   if (head_dim != 128) return IE_ERR_UNSUPPORTED;
   if (M == 0) return IE_OK;
@@ -164,7 +167,9 @@ int ie_qkv(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_di
   if (n_kv_heads > 0) {
     if ((s = check_matrix(Wk, H, H)) || (s = check_matrix(Wv, H, H))) return s;
     if (!k_cache || !v_cache) return IE_ERR_INVALID_ARG;
-    if (cache_head_stride < (int64_t)(pos0 + M) * head_dim) return IE_ERR_INVALID_ARG;
+    const int64_t rows_needed = positions ? (int64_t)cache_rows : (int64_t)(pos0 + M);
+    if (cache_head_stride < rows_needed * head_dim) return IE_ERR_INVALID_ARG;
+    if (positions && cache_batch_stride < (int64_t)n_kv_heads * cache_head_stride) return IE_ERR_INVALID_ARG;
   }
   if (!q_out) return IE_ERR_INVALID_ARG;
   cudaStream_t st = as_stream(stream);
@@ -176,6 +181,7 @@ int ie_qkv(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_di
     p.q_out = q_out; p.q_head_stride = (int64_t)M * head_dim;
     p.k_cache = k_cache; p.v_cache = v_cache; p.cache_head_stride = cache_head_stride; p.pos0 = pos0;
     p.rope_cos = rope_cos; p.rope_sin = rope_sin;
+    p.positions = positions; p.cache_batch_stride = cache_batch_stride; p.cache_rows = cache_rows;
     return from_cuda(launch_skinny(dt, EPI_QKV, p, st));
   }
   TcGemmParams q;
@@ -185,7 +191,26 @@ int ie_qkv(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_di
   q.q_out = q_out; q.q_head_stride = (int64_t)M * head_dim;
   q.k_cache = k_cache; q.v_cache = v_cache; q.cache_head_stride = cache_head_stride; q.pos0 = pos0;
   q.rope_cos = rope_cos; q.rope_sin = rope_sin;
+  q.positions = positions; q.cache_batch_stride = cache_batch_stride; q.cache_rows = cache_rows;
   return launch_tc_gemm(dt, q, st);
+}
+
+}  // namespace
+
+int ie_qkv(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_dim, const void* x, const void* Wq,
+           const void* Wk, const void* Wv, void* q_out, void* k_cache, void* v_cache, int64_t cache_head_stride,
+           int pos0, const float* rope_cos, const float* rope_sin, void* stream) {
+  return qkv_common(dt, M, H, n_q_heads, n_kv_heads, head_dim, x, Wq, Wk, Wv, q_out, k_cache, v_cache,
+                    cache_head_stride, pos0, nullptr, 0, 0, rope_cos, rope_sin, stream);
+}
+
+int ie_qkv_batched(ie_dtype dt, int B, int H, int n_q_heads, int n_kv_heads, int head_dim, const void* x,
+                   const void* Wq, const void* Wk, const void* Wv, void* q_out, void* k_cache, void* v_cache,
+                   int64_t cache_head_stride, int64_t cache_batch_stride, int cache_rows, const int* positions,
+                   const float* rope_cos, const float* rope_sin, void* stream) {
+  if (!positions || cache_rows <= 0) return IE_ERR_INVALID_ARG;
+  return qkv_common(dt, B, H, n_q_heads, n_kv_heads, head_dim, x, Wq, Wk, Wv, q_out, k_cache, v_cache,
+                    cache_head_stride, 0, positions, cache_batch_stride, cache_rows, rope_cos, rope_sin, stream);
 }
 
 size_t ie_lm_head_argmax_workspace_size(int M) {

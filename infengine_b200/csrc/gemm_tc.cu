@@ -371,16 +371,26 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
           if (head >= args.heads) break;
           T* dst;
           bool rope;
-          const int pos = p.pos0 + m;
+          int pos = p.pos0 + m;
+          bool row_ok = mvalid;
+          if (p.positions && mvalid) {
+            pos = p.positions[m];
+            if (pos < 0 || pos >= p.cache_rows) {
+              atomicExch(&g_tc_status, IE_ERR_INVALID_ARG);
+              row_ok = false;
+              pos = 0;
+            }
+          }
+          const int64_t cb = p.positions ? (int64_t)m * p.cache_batch_stride : 0;
           if (head < p.n_q_heads) {
             dst = static_cast<T*>(p.q_out) + (int64_t)head * p.q_head_stride + (int64_t)m * 128;
             rope = p.rope_cos != nullptr;
           } else if (head < p.n_q_heads + p.n_kv_heads) {
-            dst = static_cast<T*>(p.k_cache) + (int64_t)(head - p.n_q_heads) * p.cache_head_stride +
+            dst = static_cast<T*>(p.k_cache) + cb + (int64_t)(head - p.n_q_heads) * p.cache_head_stride +
                   (int64_t)pos * 128;
             rope = p.rope_cos != nullptr;
           } else {
-            dst = static_cast<T*>(p.v_cache) + (int64_t)(head - p.n_q_heads - p.n_kv_heads) * p.cache_head_stride +
+            dst = static_cast<T*>(p.v_cache) + cb + (int64_t)(head - p.n_q_heads - p.n_kv_heads) * p.cache_head_stride +
                   (int64_t)pos * 128;
             rope = false;
           }
@@ -391,7 +401,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               float x0 = round_to<T>(v[i]), x1 = round_to<T>(b[i]);
-              if (rope && mvalid) {
+              if (rope && row_ok) {
                 const int d = c * 32 + i;
                 const float cs = p.rope_cos[(int64_t)pos * 64 + d];
                 const float sn = p.rope_sin[(int64_t)pos * 64 + d];
@@ -403,7 +413,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
               v[i] = x0;
               b[i] = x1;
             }
-            if (mvalid) {
+            if (row_ok) {
               store_row32<T>(dst, c * 32, 128, v);
               store_row32<T>(dst, 64 + c * 32, 128, b);
             }

@@ -42,6 +42,10 @@ struct TcGemmParams {
   int pos0 = 0;
   const float* rope_cos = nullptr;
   const float* rope_sin = nullptr;
+  // batched rows of independent sequences (see SkinnyParams)
+  const int* positions = nullptr;
+  int64_t cache_batch_stride = 0;
+  int cache_rows = 0;
 };
 
 // Returns an IE_* status.

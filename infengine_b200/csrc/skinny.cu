@@ -68,6 +68,15 @@ constexpr int kThreads = kWarps * 32;
 #ifndef IE_SK_PERSIST
 #define IE_SK_PERSIST 0  // 1: resident CTAs walk the tiles with a grid stride
 #endif
+#ifndef IE_SK_MINBLOCKS
+#define IE_SK_MINBLOCKS 1  // __launch_bounds__ minimum resident CTAs per SM (register cap)
+#endif
+#ifndef IE_SK_EARLY_W
+#define IE_SK_EARLY_W 0  // 1: first weight batch requested before waiting for the previous kernel
+#endif
+#if IE_SK_EARLY_W && (IE_SK_PERSIST || !IE_SK_PIPE)
+#error "IE_SK_EARLY_W needs IE_SK_PIPE and no IE_SK_PERSIST"
+#endif
 constexpr int kWords = IE_SK_LOADW / 4;  // 32-bit words per lane per row per k-step
 constexpr int kStep = kWords * 2 * 4;    // k elements per step (4 lanes share a row)
 constexpr int kUnroll = IE_SK_UNROLL;
@@ -100,9 +109,10 @@ __device__ __forceinline__ const T* weight_row(const SkinnyParams& p, int tile, 
   }
 }
 
-// Device status word of the tensor-parallel exchange (IE_ERR_TIMEOUT when a
-// bounded wait for another rank's rows gave up).
-__device__ int g_tp_status = 0;
+// Device status word of the decode kernels: IE_ERR_TIMEOUT when a bounded wait
+// for another rank's rows gave up, IE_ERR_INVALID_ARG when a batched QKV row
+// carried a position outside its cache.
+__device__ int g_skinny_status = 0;
 
 // Epilogues, run by warp 0 on the fully reduced tile.
 // acc[.][mt][i]: weight row g + 8*(i>>1) of the tile, batch row m = mt*8 + 2t + (i&1).
@@ -168,7 +178,7 @@ __device__ __forceinline__ void epilogue(const SkinnyParams& p, int tile, int g,
             unsigned long long now;
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
             if (now - t0 > 2000000000ull) {
-              atomicExch(&g_tp_status, IE_ERR_TIMEOUT);
+              atomicExch(&g_skinny_status, IE_ERR_TIMEOUT);
               gave_up = true;
               break;
             }
@@ -257,7 +267,12 @@ __device__ __forceinline__ void epilogue(const SkinnyParams& p, int tile, int g,
         if (m >= p.M) continue;
         float a = round_to<T>(acc[0][mt][j]);
         float b = round_to<T>(acc[0][mt][2 + j]);
-        const int pos = p.pos0 + m;
+        const int pos = p.positions ? p.positions[m] : p.pos0 + m;
+        if (p.positions && (pos < 0 || pos >= p.cache_rows)) {
+          atomicExch(&g_skinny_status, IE_ERR_INVALID_ARG);
+          continue;
+        }
+        const int64_t cb = p.positions ? (int64_t)m * p.cache_batch_stride : 0;
         if (rope) {
           const float c = p.rope_cos[(int64_t)pos * 64 + d];
           const float s = p.rope_sin[(int64_t)pos * 64 + d];
@@ -270,9 +285,10 @@ __device__ __forceinline__ void epilogue(const SkinnyParams& p, int tile, int g,
         if (head < p.n_q_heads)
           dst = static_cast<T*>(p.q_out) + (int64_t)head * p.q_head_stride + (int64_t)m * 128;
         else if (head < p.n_q_heads + p.n_kv_heads)
-          dst = static_cast<T*>(p.k_cache) + (int64_t)(head - p.n_q_heads) * p.cache_head_stride + (int64_t)pos * 128;
+          dst = static_cast<T*>(p.k_cache) + cb + (int64_t)(head - p.n_q_heads) * p.cache_head_stride +
+                (int64_t)pos * 128;
         else
-          dst = static_cast<T*>(p.v_cache) + (int64_t)(head - p.n_q_heads - p.n_kv_heads) * p.cache_head_stride +
+          dst = static_cast<T*>(p.v_cache) + cb + (int64_t)(head - p.n_q_heads - p.n_kv_heads) * p.cache_head_stride +
                 (int64_t)pos * 128;
         dst[d] = DT<T>::from_f(a);
         dst[d + 64] = DT<T>::from_f(b);
@@ -343,7 +359,7 @@ struct Batch {
 // loads of its next batch before the MMAs of the current one, so it always
 // has loads in flight.
 template <typename T, int MT, int EPI>
-__global__ void __launch_bounds__(kThreads) skinny_kernel(const SkinnyParams p) {
+__global__ void __launch_bounds__(kThreads, IE_SK_MINBLOCKS) skinny_kernel(const SkinnyParams p) {
   constexpr int NMAT = EpiTraits<EPI>::nmat;
   constexpr int NR = NMAT * MT * 4;
   __shared__ float red[kWarps][NR][32];
@@ -364,10 +380,14 @@ __global__ void __launch_bounds__(kThreads) skinny_kernel(const SkinnyParams p) 
   const uint64_t pol = policy_evict_first();
 
   // Programmatic dependent launch: activations (X) come from the previous
-  // kernel and the outputs may be buffers it still reads, so nothing global
-  // is touched before this wait; the next kernel may be scheduled from here.
+  // kernel and the outputs may be buffers it still reads, so neither is
+  // touched before this wait; the next kernel may be scheduled from here.
+  // With IE_SK_EARLY_W the first weight batch is requested before the wait
+  // (weights are never written by the kernels this one can overlap with).
+#if !IE_SK_EARLY_W
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#endif
 
 #if IE_SK_PERSIST
   for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
@@ -391,7 +411,7 @@ __global__ void __launch_bounds__(kThreads) skinny_kernel(const SkinnyParams p) 
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[mat][mt][i] = 0.f;
 
-    auto load = [&](Batch<NMAT, MT>& b, int s) {
+    auto load_w = [&](Batch<NMAT, MT>& b, int s) {
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
         const int k = (s + u) * kStep + t * (kWords * 2);
@@ -401,9 +421,20 @@ __global__ void __launch_bounds__(kThreads) skinny_kernel(const SkinnyParams p) 
 #pragma unroll
           for (int r = 0; r < 2; ++r)
             ld_chunk<kWords>(wrow[mat][r], k, p.K, kv && rvalid[r], p.w_wide, true, pol, b.w[u][mat][r]);
+      }
+    };
+    auto load_x = [&](Batch<NMAT, MT>& b, int s) {
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int k = (s + u) * kStep + t * (kWords * 2);
+        const bool kv = s + u < s_end;
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) ld_chunk<kWords>(xrow[mt], k, p.K, kv && xvalid[mt], p.x_wide, false, pol, b.x[u][mt]);
       }
+    };
+    auto load = [&](Batch<NMAT, MT>& b, int s) {
+      load_w(b, s);
+      load_x(b, s);
     };
     auto compute = [&](const Batch<NMAT, MT>& b) {
 #pragma unroll
@@ -425,7 +456,14 @@ __global__ void __launch_bounds__(kThreads) skinny_kernel(const SkinnyParams p) 
     {
       Batch<NMAT, MT> b0, b1;
       int s = s_begin;
+#if IE_SK_EARLY_W
+      if (s < s_end) load_w(b0, s);
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+      if (s < s_end) load_x(b0, s);
+#else
       if (s < s_end) load(b0, s);
+#endif
       while (s < s_end) {
         if (s + kUnroll < s_end) load(b1, s + kUnroll);
         compute(b0);
@@ -655,12 +693,12 @@ cudaError_t launch_skinny(ie_dtype dt, int epi, const SkinnyParams& p, cudaStrea
   return cudaErrorInvalidValue;
 }
 
-int read_tp_status(bool clear) {
+int read_skinny_status(bool clear) {
   int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_tp_status, sizeof(int)) != cudaSuccess) return IE_ERR_LAUNCH;
+  if (cudaMemcpyFromSymbol(&v, g_skinny_status, sizeof(int)) != cudaSuccess) return IE_ERR_LAUNCH;
   if (clear && v) {
     const int z = 0;
-    cudaMemcpyToSymbol(g_tp_status, &z, sizeof(int));
+    cudaMemcpyToSymbol(g_skinny_status, &z, sizeof(int));
   }
   return v;
 }

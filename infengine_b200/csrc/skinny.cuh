@@ -56,6 +56,12 @@ struct SkinnyParams {
   int pos0 = 0;
   const float* rope_cos = nullptr;
   const float* rope_sin = nullptr;
+  // batched decode of independent sequences: row m at position positions[m]
+  // of its own cache (offset m * cache_batch_stride); positions outside
+  // [0, cache_rows) are skipped and reported through the device status
+  const int* positions = nullptr;
+  int64_t cache_batch_stride = 0;
+  int cache_rows = 0;
   // EPI_TP_ALLREDUCE: device array [tp_world] of every rank's symmetric
   // buffer as mapped in this process (own buffer at tp_rank)
   void* const* tp_sym = nullptr;
@@ -64,8 +70,9 @@ struct SkinnyParams {
 
 cudaError_t launch_skinny(ie_dtype dt, int epi, const SkinnyParams& p, cudaStream_t st);
 cudaError_t launch_swiglu(ie_dtype dt, int64_t n, const void* gate, const void* up, void* out, cudaStream_t st);
-// Device status word of the tensor-parallel exchange (IE_OK or IE_ERR_TIMEOUT).
-int read_tp_status(bool clear);
+// Device status word of the decode kernels (IE_OK, IE_ERR_TIMEOUT from the
+// tensor-parallel exchange, IE_ERR_INVALID_ARG from a batched QKV position).
+int read_skinny_status(bool clear);
 cudaError_t launch_argmax(ie_dtype dt, int M, int V, const void* logits, int64_t ld, int* idx_out, cudaStream_t st);
 
 }  // namespace ie

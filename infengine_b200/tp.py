@@ -218,11 +218,16 @@ class TPDecodeStep:
     """
 
     def __init__(self, plan: ShardPlan, comm: Comm, layers: list, lm_shard, rope_cos, rope_sin, pos: int,
-                 batch: int = 1, ctx: int = 8192, exchange: "P2PExchange | None" = None):
+                 batch: int = 1, ctx: int = 8192, exchange: "P2PExchange | None" = None, lm_rows: int | None = None):
         import torch
         from . import lm_head_workspace_bytes
         self.plan, self.comm, self.layers, self.lm = plan, comm, layers, lm_shard
+        if exchange is not None and batch > 16:
+            raise ValueError("the fused NVLink exchange serves decode batches of at most 16 rows")
         self.exchange = exchange
+        # rows that reach lm_head: all of them in decode, the last one in a
+        # prefill (the reference's lm_head reads row seq_len-1, lm_head.cu:7)
+        self.lm_rows = batch if lm_rows is None else lm_rows
         self.cos, self.sin, self.pos, self.ctx = rope_cos, rope_sin, pos, ctx
         dev, dt = lm_shard.device, lm_shard.dtype
         M, H = batch, plan.hidden
@@ -234,11 +239,18 @@ class TPDecodeStep:
         self.attn_out = torch.empty(M, H, device=dev, dtype=dt)
         self.h = torch.empty(M, plan.ffn_rows, device=dev, dtype=dt)
         self.ffn_out = torch.empty(M, H, device=dev, dtype=dt)
-        self.keys = torch.zeros(M, device=dev, dtype=torch.int64)
-        self.tok = torch.zeros(M, device=dev, dtype=torch.int32)
-        self.ws = torch.zeros(lm_head_workspace_bytes(M), dtype=torch.uint8, device=dev)
+        self.keys = torch.zeros(self.lm_rows, device=dev, dtype=torch.int64)
+        self.tok = torch.zeros(self.lm_rows, device=dev, dtype=torch.int32)
+        self.ws = torch.zeros(lm_head_workspace_bytes(self.lm_rows), dtype=torch.uint8, device=dev)
         # kernels of this library per step (NCCL's own kernels not counted)
         self.launches_per_step = len(layers) * (4 if exchange else 8) + 2
+
+    def flops(self) -> float:
+        """Projection FLOPs of one call on this rank (2*M*N*K per GEMM)."""
+        p, M = self.plan, self.x.shape[0]
+        H, D = p.hidden, p.head_dim
+        per_layer = ((p.q_heads + 2 * p.kv_heads) * D * H + H * p.q_heads * D + 3 * p.ffn_rows * H) * 2 * M
+        return len(self.layers) * per_layer + 2.0 * self.lm_rows * (self.lm.shape[0]) * H
 
     def __call__(self):
         from . import ffn_gate_up, lm_head_argmax, qkv
@@ -260,5 +272,6 @@ class TPDecodeStep:
             gemm_f32out(self.h, w["wd"], self.part)
             self.comm.allreduce_sum_f32(self.part)
             cast_f32(self.part, self.ffn_out)
-        lm_head_argmax(self.x, self.lm, self.ws, key_out=self.keys, vocab_offset=p.vocab_slice().start)
+        lm_head_argmax(self.x[M - self.lm_rows:], self.lm, self.ws, key_out=self.keys,
+                       vocab_offset=p.vocab_slice().start)
         self.comm.argmax_allreduce(self.keys, self.tok)

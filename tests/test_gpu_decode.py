@@ -283,3 +283,48 @@ def test_empty_and_error_paths_on_device(ie, cuda):
         ie.gemm(x, w, y, K=60, ldx=64, ldw=64)  # K % 8
     with pytest.raises(ie.IEError):
         ie.gemm(x, w, y, ldy=8)  # ldy < N
+
+
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("B", [8, 24])
+def test_qkv_batched_independent_sequences(ie, cuda, dt, B):
+    """Batched decode (BASELINE config 5 at batch 8; 24 rows run on the
+    tensor-core kernel): every row at its own position in its own cache."""
+    H, nq, nkv, hd, rows = 4096, 32, 8, 128, 512
+    d = oracle.seeded_inputs(200 + B, {"x": (B, H), "wq": (nq * hd, H), "wk": (nkv * hd, H), "wv": (nkv * hd, H)}, dt)
+    cos, sin = oracle.rope_tables(rows)
+    rng = np.random.default_rng(B)
+    pos = rng.integers(0, rows, size=B).astype(np.int32)
+    T = torch_dtype(dt)
+    q = cuda.empty((nq, B, hd), dtype=T, device="cuda")
+    kc = cuda.zeros((B, nkv, rows, hd), dtype=T, device="cuda")
+    vc = cuda.zeros((B, nkv, rows, hd), dtype=T, device="cuda")
+    ie.device_status(clear=True)
+    ie.qkv_batched(to_dev(d["x"], dt), to_dev(d["wq"], dt), to_dev(d["wk"], dt), to_dev(d["wv"], dt), q, kc, vc,
+                   cuda.from_numpy(pos).cuda(), cuda.from_numpy(cos).cuda(), cuda.from_numpy(sin).cuda())
+    assert ie.device_status(clear=True) == 0
+    got_q, got_k, got_v = from_dev(q), from_dev(kc), from_dev(vc)
+    for b in range(B):
+        qr, kr, vr = oracle.qkv(d["x"][b:b + 1], d["wq"], d["wk"], d["wv"], dt, int(pos[b]), cos, sin)
+        tq, tk, tv = rope_tol(d["x"][b:b + 1], d["wq"], d["wk"], d["wv"], dt, True)
+        assert np.all(np.abs(got_q[:, b:b + 1] - qr) <= tq)
+        assert np.all(np.abs(got_k[b][:, pos[b]:pos[b] + 1] - kr) <= tk)
+        assert np.all(np.abs(got_v[b][:, pos[b]:pos[b] + 1] - vr) <= tv)
+        others = np.ones(rows, bool)
+        others[pos[b]] = False
+        assert np.all(got_k[b][:, others] == 0)
+
+
+def test_qkv_batched_rejects_out_of_range_position(ie, cuda):
+    H, nq, nkv, rows = 4096, 32, 8, 64
+    T = cuda.bfloat16
+    x = cuda.zeros((2, H), dtype=T, device="cuda")
+    wq = cuda.zeros((nq * 128, H), dtype=T, device="cuda")
+    wk = cuda.zeros((nkv * 128, H), dtype=T, device="cuda")
+    q = cuda.empty((nq, 2, 128), dtype=T, device="cuda")
+    kc = cuda.zeros((2, nkv, rows, 128), dtype=T, device="cuda")
+    vc = cuda.zeros_like(kc)
+    pos = cuda.tensor([3, rows], dtype=cuda.int32, device="cuda")  # second row out of range
+    ie.device_status(clear=True)
+    ie.qkv_batched(x, wq, wk, wk, q, kc, vc, pos)
+    assert ie.device_status(clear=True) == -1  # IE_ERR_INVALID_ARG, row skipped
