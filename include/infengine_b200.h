@@ -77,6 +77,16 @@ int ie_gemm(ie_dtype dt, int M, int N, int K,
             void* Y, int64_t ldy,
             void* stream);
 
+/* Same product followed by the residual add of the decode / prefill loop
+ * (decode.cu:28,38 with kernels/residual_add.cu:10-20): Y = round(Y +
+ * round(X . W^T)), in place on the residual stream Y. No single counterpart in
+ * the reference (there: the projection, then residual_add). */
+int ie_gemm_add(ie_dtype dt, int M, int N, int K,
+                const void* X, int64_t ldx,
+                const void* W, int64_t ldw,
+                void* Y, int64_t ldy,
+                void* stream);
+
 /* Same projection with unrounded fp32 output Y[M,N] (row stride ldy floats,
  * 16-byte aligned): the partial sums of a row-split (tensor-parallel) O or
  * down projection, to be summed across ranks before the one rounding. */
@@ -129,7 +139,8 @@ int ie_ffn_gate_up(ie_dtype dt, int M, int H, int F,
  *   v_cache same layout as k_cache.
  * Wq: [n_q_heads*head_dim, H], Wk/Wv: [n_kv_heads*head_dim, H].
  * RoPE (rotate-half, pairs (d, d+head_dim/2), table rows = position,
- * table [*, head_dim/2] fp32) is applied to Q and K at position pos0 + m.
+ * table [*, head_dim/2] fp32, 16-byte aligned) is applied to Q and K at
+ * position pos0 + m.
  * head_dim must be 128 (the Llama-3.1 value, config.h:16).
  */
 int ie_qkv(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_dim,
@@ -168,6 +179,25 @@ int ie_attention(ie_dtype dt, int S, int pos0, int n_q_heads, int n_kv_heads, in
                  const void* q, int64_t q_head_stride,
                  const void* k_cache, const void* v_cache, int64_t cache_head_stride,
                  void* out, int64_t ld_out, void* stream);
+
+/* Decode-time attention (same chain as ie_attention) for R query rows that
+ * each read their whole cache, split over the GPU: every (row, KV head) is
+ * served by a cluster of 8 CTAs, each over 1/8 of the cache rows, merged
+ * through distributed shared memory. Row m belongs to sequence
+ * m / rows_per_seq (cache at + that * cache_batch_stride elements) and sits at
+ * position positions[m] (device array, R entries; read when the kernel runs,
+ * so a captured graph follows it) or, when positions is NULL, pos0 + m; it
+ * attends cache rows 0 .. its position. q [n_q_heads][R][128] (head stride
+ * q_head_stride), out [R][n_q_heads*128] (row stride ld_out). A position
+ * outside [0, cache_rows) writes zeros and sets IE_ERR_INVALID_ARG in
+ * ie_device_status. n_q_heads / n_kv_heads in {1, 2, 4, 8}; cache_rows *
+ * group <= ~270k. The reference has no batched or device-positioned form of
+ * this (decode_attn, kernels/attn.cu:390-439, serves one row). */
+int ie_attention_decode(ie_dtype dt, int R, int rows_per_seq, int n_q_heads, int n_kv_heads, int head_dim,
+                        const void* q, int64_t q_head_stride,
+                        const void* k_cache, const void* v_cache, int64_t cache_head_stride,
+                        int64_t cache_batch_stride, int cache_rows, const int* positions, int pos0,
+                        void* out, int64_t ld_out, void* stream);
 
 /* ---- a6 + a7: lm_head with fused greedy argmax --------------------------
  * Replaces lm_head (kernels/lm_head.cu:5-20) followed by sample_token_amax
@@ -272,6 +302,10 @@ int ie_ipc_release(void* dev_ptr);
 int ie_gemm_allreduce(ie_dtype dt, int M, int N, int K,
                       const void* X, int64_t ldx, const void* W, int64_t ldw,
                       void* Y, int64_t ldy, const ie_tp_exchange* ex, void* stream);
+/* The same with the residual add fused: Y = round(Y + round(sum over ranks)). */
+int ie_gemm_allreduce_add(ie_dtype dt, int M, int N, int K,
+                          const void* X, int64_t ldx, const void* W, int64_t ldw,
+                          void* Y, int64_t ldy, const ie_tp_exchange* ex, void* stream);
 
 /* Global vocabulary id held in a packed argmax key. */
 static inline int ie_argmax_key_index(unsigned long long key) {

@@ -56,6 +56,7 @@ EXPORTED_SYMBOLS = (
     "ie_lm_head_argmax_noalloc", "ie_attention", "ie_gemm_f32out", "ie_comm_unique_id", "ie_comm_create",
     "ie_comm_destroy", "ie_allreduce_sum_f32", "ie_argmax_allreduce", "ie_cast_f32", "ie_tp_exchange_bytes",
     "ie_ipc_export", "ie_ipc_import", "ie_ipc_release", "ie_gemm_allreduce", "ie_qkv_batched",
+    "ie_attention_decode", "ie_gemm_add", "ie_gemm_allreduce_add",
 )
 
 
@@ -82,6 +83,8 @@ def lib() -> ctypes.CDLL:
         L.ie_device_status.argtypes = [i32]
         L.ie_device_status.restype = i32
         L.ie_gemm.argtypes = [i32, i32, i32, i32, vp, i64, vp, i64, vp, i64, vp]
+        L.ie_gemm_add.argtypes = [i32, i32, i32, i32, vp, i64, vp, i64, vp, i64, vp]
+        L.ie_gemm_add.restype = i32
         L.ie_swiglu.argtypes = [i32, i32, i32, vp, vp, vp, vp]
         L.ie_ffn_workspace_size.restype = sz
         L.ie_ffn_workspace_size.argtypes = [i32, i32]
@@ -98,6 +101,9 @@ def lib() -> ctypes.CDLL:
         L.ie_argmax.argtypes = [i32, i32, i32, vp, i64, vp, vp]
         L.ie_attention.argtypes = [i32, i32, i32, i32, i32, i32, vp, i64, vp, vp, i64, vp, i64, vp]
         L.ie_attention.restype = i32
+        L.ie_attention_decode.argtypes = [i32, i32, i32, i32, i32, i32, vp, i64, vp, vp, i64, i64, i32, vp, i32, vp,
+                                          i64, vp]
+        L.ie_attention_decode.restype = i32
         L.ie_lm_head_argmax_noalloc.argtypes = [i32, i32, i32, i32, i64, vp, i64, vp, vp, i64, vp, vp, vp]
         L.ie_lm_head_argmax_noalloc.restype = i32
         for name in ("ie_gemm", "ie_swiglu", "ie_ffn", "ie_qkv", "ie_lm_head_argmax", "ie_argmax"):
@@ -143,6 +149,15 @@ def _check(status: int, what: str) -> None:
 
 
 # -------------------------------------------------------------- C-ABI mirror
+def gemm_add(x, w, y, stream=None):
+    """y[M,N] = round(y + round(x[M,K] . w[N,K]^T)) in place (ie_gemm_add):
+    a projection with the residual add fused."""
+    M, K = x.shape
+    N = w.shape[0]
+    _check(lib().ie_gemm_add(_dt(x), M, N, K, _ptr(x), x.stride(0), _ptr(w), w.stride(0), _ptr(y), y.stride(0),
+                             _stream(stream)), "ie_gemm_add")
+
+
 def gemm(x, w, y, M=None, N=None, K=None, ldx=None, ldw=None, ldy=None, stream=None):
     """y[M,N] = x[M,K] . w[N,K]^T (ie_gemm)."""
     M = x.shape[0] if M is None else M
@@ -187,6 +202,24 @@ def attention(q, k_cache, v_cache, out, pos0, n_kv_heads=NUM_KV_HEADS, stream=No
     nq, S, D = q.shape
     _check(lib().ie_attention(_dt(q), S, pos0, nq, n_kv_heads, D, _ptr(q), q.stride(0), _ptr(k_cache), _ptr(v_cache),
                               k_cache.stride(0), _ptr(out), out.stride(0), _stream(stream)), "ie_attention")
+
+
+def attention_decode(q, k_cache, v_cache, out, positions=None, pos0=0, rows_per_seq=None, stream=None):
+    """ie_attention_decode: q [nq, R, 128] head-major; caches [nkv, rows, 128]
+    (one sequence) or [B, nkv, rows, 128] (row m belongs to sequence
+    m // rows_per_seq); positions: device int32 [R] or None (row m at pos0 + m);
+    out [R, nq*128]."""
+    nq, R, D = q.shape
+    if k_cache.dim() == 4:
+        B, nkv, rows = k_cache.shape[:3]
+        cbs, chs = k_cache.stride(0), k_cache.stride(1)
+    else:
+        B, (nkv, rows) = 1, k_cache.shape[:2]
+        cbs, chs = 0, k_cache.stride(0)
+    rps = rows_per_seq if rows_per_seq is not None else max(R // B, 1)
+    _check(lib().ie_attention_decode(_dt(q), R, rps, nq, nkv, D, _ptr(q), q.stride(0), _ptr(k_cache), _ptr(v_cache),
+                                     chs, cbs, rows, _ptr(positions), pos0, _ptr(out), out.stride(0),
+                                     _stream(stream)), "ie_attention_decode")
 
 
 def qkv_batched(x, wq, wk, wv, q_out, k_cache, v_cache, positions, rope_cos=None, rope_sin=None,

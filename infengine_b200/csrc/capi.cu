@@ -4,6 +4,7 @@
 #include "ie_common.cuh"
 #include "skinny.cuh"
 #include "gemm_tc.cuh"
+#include "attention.cuh"
 
 using namespace ie;
 
@@ -56,11 +57,12 @@ int ie_device_status(int clear) {
   if (cudaDeviceSynchronize() != cudaSuccess) return IE_ERR_LAUNCH;
   const int a = read_tc_status(clear != 0);
   const int b = read_skinny_status(clear != 0);
-  return a != IE_OK ? a : b;
+  const int c = read_attn_status(clear != 0);
+  return a != IE_OK ? a : (b != IE_OK ? b : c);
 }
 
-int ie_gemm(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, void* Y,
-            int64_t ldy, void* stream) {
+static int gemm_store(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw,
+                      void* Y, int64_t ldy, bool residual, void* stream) {
   if (!valid_dtype(dt) || M < 0 || N < 0 || K <= 0) return IE_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return IE_OK;
   if (K % 8) return IE_ERR_ALIGNMENT;
@@ -71,13 +73,25 @@ int ie_gemm(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const 
     SkinnyParams p;
     p.X = X; p.ldx = ldx; p.M = M; p.N = N; p.K = K;
     p.W0 = W; p.ldw = ldw; p.Y = Y; p.ldy = ldy;
+    p.residual = residual;
     return from_cuda(launch_skinny(dt, EPI_STORE, p, as_stream(stream)));
   }
   if ((s = check_matrix(Y, ldy, N))) return s;
   TcGemmParams q;
   q.A = X; q.lda = ldx; q.B = W; q.ldb = ldw; q.M = M; q.N = N; q.K = K;
   q.D = Y; q.ldd = ldy; q.epi = TC_EPI_STORE;
+  q.residual = residual;
   return launch_tc_gemm(dt, q, as_stream(stream));
+}
+
+int ie_gemm(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, void* Y,
+            int64_t ldy, void* stream) {
+  return gemm_store(dt, M, N, K, X, ldx, W, ldw, Y, ldy, false, stream);
+}
+
+int ie_gemm_add(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, void* Y,
+                int64_t ldy, void* stream) {
+  return gemm_store(dt, M, N, K, X, ldx, W, ldw, Y, ldy, true, stream);
 }
 
 int ie_gemm_f32out(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, float* Y,
@@ -162,6 +176,7 @@ int qkv_common(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int hea
   if (M == 0) return IE_OK;
   if (H % 8) return IE_ERR_ALIGNMENT;
   if ((rope_cos == nullptr) != (rope_sin == nullptr)) return IE_ERR_INVALID_ARG;
+  if (rope_cos && (!aligned16(rope_cos) || !aligned16(rope_sin))) return IE_ERR_ALIGNMENT;
   int s;
   if ((s = check_matrix(x, H, H)) || (s = check_matrix(Wq, H, H))) return s;
   if (n_kv_heads > 0) {

@@ -155,21 +155,26 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 // Store 32 consecutive values of one output row (columns col0.. col0+31,
 // those < ncols), 16-byte vectors when the whole chunk is in range.
+// With `add`, the stored value is round(old + round(v)) (residual add).
 template <typename T>
-__device__ __forceinline__ void store_row32(T* dst, int col0, int ncols, const float (&v)[32]) {
+__device__ __forceinline__ void store_row32(T* dst, int col0, int ncols, const float (&v)[32], bool add = false) {
   if (col0 + 32 <= ncols) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      uint4 pk;
+      uint4 pk, old;
+      if (add) old = *reinterpret_cast<const uint4*>(dst + col0 + j * 8);
+      const T* o = reinterpret_cast<const T*>(&old);
       T* e = reinterpret_cast<T*>(&pk);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) e[i] = DT<T>::from_f(v[j * 8 + i]);
+      for (int i = 0; i < 8; ++i)
+        e[i] = DT<T>::from_f(add ? DT<T>::to_f(o[i]) + round_to<T>(v[j * 8 + i]) : v[j * 8 + i]);
       *reinterpret_cast<uint4*>(dst + col0 + j * 8) = pk;
     }
   } else {
 #pragma unroll
     for (int i = 0; i < 32; ++i)
-      if (col0 + i < ncols) dst[col0 + i] = DT<T>::from_f(v[i]);
+      if (col0 + i < ncols)
+        dst[col0 + i] = DT<T>::from_f(add ? DT<T>::to_f(dst[col0 + i]) + round_to<T>(v[i]) : v[i]);
   }
 }
 
@@ -347,7 +352,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           tmem_ld32(tbase + c * 32, v);
-          if (mvalid) store_row32<T>(drow, nb * BN + c * 32, p.N, v);
+          if (mvalid) store_row32<T>(drow, nb * BN + c * 32, p.N, v, p.residual);
         }
       } else if constexpr (EPI == TC_EPI_SWIGLU) {
         T* drow = static_cast<T*>(p.D) + (int64_t)m * p.ldd;
@@ -398,15 +403,25 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
           for (int c = 0; c < 2; ++c) {
             tmem_ld32(tbase + h * 128 + c * 32, v);       // d in [32c, 32c+32)
             tmem_ld32(tbase + h * 128 + 64 + c * 32, b);  // d + 64
+            // this row's 32 table entries, as 16-byte vectors (tables are
+            // 16-byte aligned and rows are 256 bytes)
+            float cs[32], sn[32];
+            if (rope && row_ok) {
+              const float4* cp = reinterpret_cast<const float4*>(p.rope_cos + (int64_t)pos * 64 + c * 32);
+              const float4* sp = reinterpret_cast<const float4*>(p.rope_sin + (int64_t)pos * 64 + c * 32);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 a4 = __ldg(cp + j), b4 = __ldg(sp + j);
+                cs[4 * j] = a4.x; cs[4 * j + 1] = a4.y; cs[4 * j + 2] = a4.z; cs[4 * j + 3] = a4.w;
+                sn[4 * j] = b4.x; sn[4 * j + 1] = b4.y; sn[4 * j + 2] = b4.z; sn[4 * j + 3] = b4.w;
+              }
+            }
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               float x0 = round_to<T>(v[i]), x1 = round_to<T>(b[i]);
               if (rope && row_ok) {
-                const int d = c * 32 + i;
-                const float cs = p.rope_cos[(int64_t)pos * 64 + d];
-                const float sn = p.rope_sin[(int64_t)pos * 64 + d];
-                const float y0 = x0 * cs - x1 * sn;
-                const float y1 = x0 * sn + x1 * cs;
+                const float y0 = x0 * cs[i] - x1 * sn[i];
+                const float y1 = x0 * sn[i] + x1 * cs[i];
                 x0 = y0;
                 x1 = y1;
               }

@@ -26,6 +26,8 @@ struct TcGemmParams {
   void* D = nullptr;
   int64_t ldd = 0;
   int epi = TC_EPI_STORE;
+  // TC_EPI_STORE: D = round(D + round(acc)) (residual add after O / down)
+  bool residual = false;
   // TC_EPI_ARGMAX
   int64_t vocab_offset = 0;
   unsigned long long* keys = nullptr;

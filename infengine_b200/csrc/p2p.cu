@@ -89,8 +89,8 @@ int ie_ipc_release(void* ptr) {
   return IE_ERR_INVALID_ARG;
 }
 
-int ie_gemm_allreduce(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw,
-                      void* Y, int64_t ldy, const ie_tp_exchange* ex, void* stream) {
+static int gemm_allreduce(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw,
+                          void* Y, int64_t ldy, const ie_tp_exchange* ex, bool residual, void* stream) {
   if ((dt != IE_DTYPE_F16 && dt != IE_DTYPE_BF16) || M < 0 || N < 0 || K <= 0 || !ex) return IE_ERR_INVALID_ARG;
   if (ex->world < 1 || ex->world > kTpMaxWorld || ex->rank < 0 || ex->rank >= ex->world || !ex->sym)
     return IE_ERR_INVALID_ARG;
@@ -104,9 +104,20 @@ int ie_gemm_allreduce(ie_dtype dt, int M, int N, int K, const void* X, int64_t l
   p.W0 = W; p.ldw = ldw; p.Y = Y; p.ldy = ldy;
   p.tp_sym = ex->sym; p.tp_world = ex->world; p.tp_rank = ex->rank;
   p.tp_rows = ex->max_rows; p.tp_cols = ex->max_cols;
+  p.residual = residual;
   return launch_skinny(dt, EPI_TP_ALLREDUCE, p, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess
              ? IE_OK
              : IE_ERR_LAUNCH;
+}
+
+int ie_gemm_allreduce(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw,
+                      void* Y, int64_t ldy, const ie_tp_exchange* ex, void* stream) {
+  return gemm_allreduce(dt, M, N, K, X, ldx, W, ldw, Y, ldy, ex, false, stream);
+}
+
+int ie_gemm_allreduce_add(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw,
+                          void* Y, int64_t ldy, const ie_tp_exchange* ex, void* stream) {
+  return gemm_allreduce(dt, M, N, K, X, ldx, W, ldw, Y, ldy, ex, true, stream);
 }
 
 }  // extern "C"

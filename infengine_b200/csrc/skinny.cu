@@ -184,7 +184,10 @@ __device__ __forceinline__ void epilogue(const SkinnyParams& p, int tile, int g,
             }
           }
         }
-        if (!gave_up) Y[(int64_t)m * p.ldy + nidx[r]] = DT<T>::from_f(sum);
+        if (!gave_up) {
+          T* y = Y + (int64_t)m * p.ldy + nidx[r];
+          *y = DT<T>::from_f(p.residual ? DT<T>::to_f(*y) + round_to<T>(sum) : sum);
+        }
       }
   } else if constexpr (EPI == EPI_STORE_F32) {
     float* Y = static_cast<float*>(p.Y);
@@ -202,7 +205,10 @@ __device__ __forceinline__ void epilogue(const SkinnyParams& p, int tile, int g,
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int r = i >> 1, m = mt * 8 + 2 * t + (i & 1);
-        if (rvalid[r] && m < p.M) Y[(int64_t)m * p.ldy + nidx[r]] = DT<T>::from_f(acc[0][mt][i]);
+        if (rvalid[r] && m < p.M) {
+          T* y = Y + (int64_t)m * p.ldy + nidx[r];
+          *y = DT<T>::from_f(p.residual ? DT<T>::to_f(*y) + round_to<T>(acc[0][mt][i]) : acc[0][mt][i]);
+        }
       }
   } else if constexpr (EPI == EPI_SWIGLU) {
     T* Y = static_cast<T*>(p.Y);

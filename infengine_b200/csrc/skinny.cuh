@@ -40,6 +40,9 @@ struct SkinnyParams {
   int tiles = 0;
   void* Y = nullptr;
   int64_t ldy = 0;
+  // EPI_STORE / EPI_TP_ALLREDUCE: Y = round(Y + round(result)), the residual
+  // add that follows the O and down projections
+  bool residual = false;
   // EPI_ARGMAX
   int64_t vocab_offset = 0;
   unsigned long long* keys = nullptr;

@@ -153,8 +153,9 @@ class P2PExchange:
         L.ie_ipc_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)]
         L.ie_ipc_import.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]
         L.ie_ipc_release.argtypes = [ctypes.c_void_p]
-        L.ie_gemm_allreduce.argtypes = [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_int64] * 3 + [
-            ctypes.POINTER(_Exchange), ctypes.c_void_p]
+        for fn in (L.ie_gemm_allreduce, L.ie_gemm_allreduce_add):
+            fn.argtypes = [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_int64] * 3 + [
+                ctypes.POINTER(_Exchange), ctypes.c_void_p]
         nbytes = int(L.ie_tp_exchange_bytes(world, max_rows, max_cols))
         self.buf = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
         torch.cuda.synchronize()
@@ -179,12 +180,14 @@ class P2PExchange:
         self.desc = _Exchange(world, rank, ctypes.c_void_p(self.sym.data_ptr()), max_rows, max_cols)
         dist.barrier(group=group)
 
-    def gemm_allreduce(self, x, w, y, stream=None):
-        """y[M,N] = round(sum over ranks of x_r . w_r^T), one fused kernel."""
+    def gemm_allreduce(self, x, w, y, stream=None, residual=False):
+        """y[M,N] = round(sum over ranks of x_r . w_r^T), one fused kernel;
+        with residual, y = round(y + round(sum)) in place."""
         M, K = x.shape
         N = w.shape[0]
-        _check(lib().ie_gemm_allreduce(_dt(x), M, N, K, _ptr(x), x.stride(0), _ptr(w), w.stride(0), _ptr(y),
-                                       y.stride(0), ctypes.byref(self.desc), _stream(stream)), "ie_gemm_allreduce")
+        fn = lib().ie_gemm_allreduce_add if residual else lib().ie_gemm_allreduce
+        _check(fn(_dt(x), M, N, K, _ptr(x), x.stride(0), _ptr(w), w.stride(0), _ptr(y), y.stride(0),
+                  ctypes.byref(self.desc), _stream(stream)), "ie_gemm_allreduce")
 
     def close(self):
         for p in self.imported:

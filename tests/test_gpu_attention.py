@@ -29,3 +29,75 @@ def test_attention_core(ie, cuda, dt, S, pos0, nq, nkv):
     err = np.abs(got - want)
     assert np.all(err <= 2 * ulp(want, dt) + 0.02 * np.abs(want).max()), err.max()
     assert oracle.normwise_rel_err(got, want) < (5e-3 if dt == "f16" else 2e-2)
+
+
+def _check_close(got, want, dt):
+    err = np.abs(got - want)
+    assert not np.isnan(got).any()
+    assert np.all(err <= 2 * ulp(want, dt) + 0.02 * np.abs(want).max()), err.max()
+    assert oracle.normwise_rel_err(got, want) < (5e-3 if dt == "f16" else 2e-2)
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("pos,nq,nkv,rows", [(0, 32, 8, 2048), (5, 32, 8, 2048), (300, 32, 8, 2048),
+                                             (2047, 32, 8, 2048), (8191, 32, 8, 8192), (1000, 8, 8, 1024),
+                                             (777, 16, 2, 1024), (130, 8, 4, 256)])
+def test_attention_decode_one_row(ie, cuda, dt, pos, nq, nkv, rows):
+    """Split-KV decode attention, one query row over its whole cache (slices
+    of fewer than 8 rows, exact 64-row chunks, ragged tails, groups 1-8)."""
+    rng = np.random.default_rng(pos * 7 + nq + rows)
+    q = oracle.round_dt(rng.standard_normal((nq, 1, 128), dtype=np.float32), dt)
+    k = np.zeros((nkv, rows, 128), np.float32)
+    v = np.zeros((nkv, rows, 128), np.float32)
+    k[:, :pos + 1] = oracle.round_dt(rng.standard_normal((nkv, pos + 1, 128), dtype=np.float32), dt)
+    v[:, :pos + 1] = oracle.round_dt(rng.standard_normal((nkv, pos + 1, 128), dtype=np.float32), dt)
+    out = cuda.full((1, nq * 128), float("nan"), dtype=torch_dtype(dt), device="cuda")
+    positions = cuda.tensor([pos], dtype=cuda.int32, device="cuda")
+    ie.attention_decode(to_dev(q, dt), to_dev(k, dt), to_dev(v, dt), out, positions=positions)
+    assert ie.device_status() == 0
+    _check_close(from_dev(out), oracle.attention(q, k, v, pos, dt), dt)
+
+
+@pytest.mark.parametrize("dt", ["bf16"])
+def test_attention_decode_batched_and_verify(ie, cuda, dt):
+    """Eight sequences with their own positions (batched decode), then five
+    causal rows of one sequence (speculative verify, positions from pos0)."""
+    rng = np.random.default_rng(3)
+    B, nq, nkv, rows = 8, 32, 8, 1024
+    pos = np.array([0, 1, 63, 64, 500, 1000, 1023, 7], dtype=np.int32)
+    q = oracle.round_dt(rng.standard_normal((nq, B, 128), dtype=np.float32), dt)
+    k = oracle.round_dt(rng.standard_normal((B, nkv, rows, 128), dtype=np.float32), dt)
+    v = oracle.round_dt(rng.standard_normal((B, nkv, rows, 128), dtype=np.float32), dt)
+    out = cuda.full((B, nq * 128), float("nan"), dtype=torch_dtype(dt), device="cuda")
+    ie.attention_decode(to_dev(q, dt), to_dev(k, dt), to_dev(v, dt), out,
+                        positions=cuda.from_numpy(pos).cuda())
+    assert ie.device_status() == 0
+    got = from_dev(out)
+    for b in range(B):
+        want = oracle.attention(q[:, b:b + 1], k[b], v[b], int(pos[b]), dt)
+        _check_close(got[b:b + 1], want, dt)
+    # verify pass: 5 rows of sequence 0 at positions 900..904
+    qv = oracle.round_dt(rng.standard_normal((nq, 5, 128), dtype=np.float32), dt)
+    outv = cuda.full((5, nq * 128), float("nan"), dtype=torch_dtype(dt), device="cuda")
+    ie.attention_decode(to_dev(qv, dt), to_dev(k[0], dt), to_dev(v[0], dt), outv, pos0=900, rows_per_seq=5)
+    assert ie.device_status() == 0
+    _check_close(from_dev(outv), oracle.attention(qv, k[0], v[0], 900, dt), dt)
+
+
+def test_attention_decode_bad_position(ie, cuda):
+    """A device position outside the cache: that row is zero, the status word
+    says IE_ERR_INVALID_ARG, the other rows are unaffected."""
+    dt = "bf16"
+    rng = np.random.default_rng(5)
+    nq, nkv, rows = 8, 2, 256
+    q = oracle.round_dt(rng.standard_normal((nq, 2, 128), dtype=np.float32), dt)
+    k = oracle.round_dt(rng.standard_normal((2, nkv, rows, 128), dtype=np.float32), dt)
+    v = oracle.round_dt(rng.standard_normal((2, nkv, rows, 128), dtype=np.float32), dt)
+    out = cuda.full((2, nq * 128), float("nan"), dtype=torch_dtype(dt), device="cuda")
+    pos = cuda.tensor([100, rows], dtype=cuda.int32, device="cuda")
+    ie.attention_decode(to_dev(q, dt), to_dev(k, dt), to_dev(v, dt), out, positions=pos)
+    assert ie.device_status() == -1  # IE_ERR_INVALID_ARG
+    got = from_dev(out)
+    assert np.all(got[1] == 0)
+    _check_close(got[0:1], oracle.attention(q[:, 0:1], k[0], v[0], 100, dt), dt)
+    assert ie.device_status() == 0  # cleared by the read above
