@@ -307,6 +307,66 @@ int ie_gemm_allreduce_add(ie_dtype dt, int M, int N, int K,
                           const void* X, int64_t ldx, const void* W, int64_t ldw,
                           void* Y, int64_t ldy, const ie_tp_exchange* ex, void* stream);
 
+/* ---- glue of a complete decode step -----------------------------------------
+ * RMSNorm with the reference's arithmetic (kernels/rmsnorm.cu:29-62: the same
+ * 1024-way partial sums and halving tree, rsqrt(sum / H + eps), out =
+ * round(round(x * scale) * w)); out may alias x. */
+int ie_rmsnorm(ie_dtype dt, int M, int H, const void* x, int64_t ldx, const void* w,
+               void* out, int64_t ldo, float eps, void* stream);
+/* Embedding rows (kernels/emblookup.cu:12-27): out[m] = table[tokens[m]],
+ * tokens a device array [M]; a token outside [0, vocab) gives a zero row and
+ * IE_ERR_INVALID_ARG in ie_device_status. H % 8 == 0. */
+int ie_embed(ie_dtype dt, int M, int H, int vocab, const int* tokens, const void* table,
+             void* out, int64_t ldo, void* stream);
+
+/* ---- decode engine ------------------------------------------------------------
+ * The reference's request flow (manager.cpp:31-86: prefill, then greedy
+ * decode_step in a loop, prefill.cu:11-48, decode.cu:11-49) on this library's
+ * kernels. Weights are the caller's device pointers, laid out like the
+ * reference's ModelWeights (kernels/model_weights.cuh:7-34), in dt. The
+ * engine owns its activations, the KV caches of max_batch sequences
+ * (max_ctx positions each) and a CUDA graph of one decode step: a step runs
+ * every sequence one token forward with positions and tokens kept on the
+ * device, so n steps are n graph launches and one copy of the ids. */
+typedef struct ie_llama_layer_weights {
+  const void* attn_norm;                 /* [H]                         input_layernorm   */
+  const void *wq, *wk, *wv;              /* [nq*128, H], [nkv*128, H] x2 transformer.w_q.. */
+  const void* wo;                        /* [H, nq*128]                 transformer.w_o   */
+  const void* ffn_norm;                  /* [H]                   post_attention_layernorm */
+  const void *w_gate, *w_up;             /* [F, H]                      ffn_block         */
+  const void* w_down;                    /* [H, F]                                        */
+} ie_llama_layer_weights;
+typedef struct ie_llama_desc {
+  int n_layers, hidden, n_q_heads, n_kv_heads, head_dim, ffn_dim, vocab;
+  float rms_eps;
+  const void* embedding;                 /* [vocab, H]                                    */
+  const ie_llama_layer_weights* layers;  /* host array [n_layers] (copied at create)      */
+  const void* final_norm;                /* [H]                                           */
+  const void* lm_head;                   /* [vocab, H]                                    */
+  const float *rope_cos, *rope_sin;      /* device [>= max_ctx][head_dim/2], 16-B aligned */
+} ie_llama_desc;
+typedef struct ie_engine ie_engine;
+/* stream NULL: the engine makes its own non-blocking stream. max_prefill is
+ * the longest chunk ie_engine_prefill accepts. */
+int ie_engine_create(ie_dtype dt, const ie_llama_desc* desc, int max_batch, int max_ctx, int max_prefill,
+                     void* stream, ie_engine** out);
+int ie_engine_destroy(ie_engine* eng);
+/* Append n tokens (host array) to sequence seq from its current position;
+ * the greedy next token becomes the sequence's next input (and *next_token,
+ * when non-NULL). Blocks until done. */
+int ie_engine_prefill(ie_engine* eng, int seq, const int* tokens, int n, int* next_token);
+/* n_steps greedy steps of all max_batch sequences; out_tokens (host,
+ * nullable) receives [n_steps][max_batch] ids. Blocks until done. */
+int ie_engine_decode(ie_engine* eng, int n_steps, int* out_tokens);
+/* Speculative verify: M <= 16 tokens (host) of sequence seq at positions
+ * pos .. pos+M-1 (pos = its current position) in one pass; out_ids[m] is the
+ * greedy id after row m. The cache rows are written; the position is not
+ * moved (ie_engine_set_position accepts a prefix). */
+int ie_engine_verify(ie_engine* eng, int seq, const int* tokens, int M, int* out_ids);
+int ie_engine_set_position(ie_engine* eng, int seq, int pos, int next_token);
+int ie_engine_position(const ie_engine* eng, int seq);
+void* ie_engine_stream(const ie_engine* eng);
+
 /* Global vocabulary id held in a packed argmax key. */
 static inline int ie_argmax_key_index(unsigned long long key) {
   unsigned int tie = ~(unsigned int)(key & 0xffffffffull);

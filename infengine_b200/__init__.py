@@ -56,7 +56,9 @@ EXPORTED_SYMBOLS = (
     "ie_lm_head_argmax_noalloc", "ie_attention", "ie_gemm_f32out", "ie_comm_unique_id", "ie_comm_create",
     "ie_comm_destroy", "ie_allreduce_sum_f32", "ie_argmax_allreduce", "ie_cast_f32", "ie_tp_exchange_bytes",
     "ie_ipc_export", "ie_ipc_import", "ie_ipc_release", "ie_gemm_allreduce", "ie_qkv_batched",
-    "ie_attention_decode", "ie_gemm_add", "ie_gemm_allreduce_add",
+    "ie_attention_decode", "ie_gemm_add", "ie_gemm_allreduce_add", "ie_rmsnorm", "ie_embed", "ie_engine_create",
+    "ie_engine_destroy", "ie_engine_prefill", "ie_engine_decode", "ie_engine_verify", "ie_engine_set_position",
+    "ie_engine_position", "ie_engine_stream",
 )
 
 

@@ -28,7 +28,8 @@ CFLAGS = ARCH + [
     "-I", str(ROOT / "include"), "--expt-relaxed-constexpr",
 ]
 
-CORE_SOURCES = ["capi.cu", "skinny.cu", "gemm_tc.cu", "noalloc.cu", "comm.cu", "attention.cu", "p2p.cu"]
+CORE_SOURCES = ["capi.cu", "skinny.cu", "gemm_tc.cu", "noalloc.cu", "comm.cu", "attention.cu", "p2p.cu", "norm.cu",
+                "engine.cu"]
 DROPIN_SOURCES = ["dropin.cu"]
 
 LIB_CORE = PKG / "libinfengine_b200.so"

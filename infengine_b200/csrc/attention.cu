@@ -1,4 +1,5 @@
-// Attention core behind the drop-in attn / decode_attn entry points.
+// Attention core behind the drop-in attn / decode_attn entry points and the
+// decode engine.
 //
 // Not a weight matmul: it exists so that the reference's attention entry
 // points (kernels/attn.cuh:5-8), whose translation unit also holds the Q/K/V
@@ -7,194 +8,25 @@
 // [S, n_q_heads * 128] output the O projection consumes (the layout the
 // reference produces with attn_permute, kernels/attn_permute.cu:15-32).
 //
-// Numerics follow the reference's chain (kernels/attn.cu:355-366,
+// The reference's chain (kernels/attn.cu:355-366, :423-431,
 // kernels/softmax.cu:55-160): a score is one fp32 dot product rounded to the
 // storage type (the cuBLAS QK^T output), scaled by rsqrt(128) and rounded
-// again; the row maximum is taken over those values; e = exp(t - max) is
-// summed in fp32 and stored rounded; p = round(round(e) / sum); the output is
-// one fp32 accumulation of p * V rounded once (the cuBLAS A.V output).
-//
-// One CTA per (KV head, query row) serves the n_q_heads / n_kv_heads query
-// heads that share the KV head (grouped-query attention reads K and V once
-// for all of them). Causal: query row s at position pos0 + s attends to
-// positions 0 .. pos0 + s. Scores of a row live in shared memory (up to
-// group * (pos0 + S) floats).
+// again; e = exp(t - max) is summed in fp32 and stored rounded;
+// p = round(round(e) * (1/sum)); out = round(p.V) (one fp32 accumulation).
+// Two kernels:
+//  * few query rows (decode, verify): split-KV over a thread-block cluster,
+//    which keeps the chain exactly (exact row max and sum before any p);
+//  * many query rows (prefill): a flash-attention kernel on the tensor cores
+//    (mma.sync m16n8k16, fp32 accumulation) with the same roundings of s, t
+//    and p, but the running-maximum form of the softmax: p is round(e) with
+//    e taken against the running maximum, and the division by the sum comes
+//    after the p.V accumulation. Its outputs differ from the chain by about a
+//    rounding step of p.
 #include <climits>
 #include <cstdlib>
+#include <type_traits>
 #include "ie_common.cuh"
 #include "attention.cuh"
-
-namespace ie {
-namespace {
-
-constexpr int kAttnThreads = 256;
-constexpr int kMaxGroup = 8;
-
-template <typename T>
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const T* __restrict__ q, int64_t q_head_stride,
-                                                                  const T* __restrict__ kc,
-                                                                  const T* __restrict__ vc, int64_t chs, int pos0,
-                                                                  int group, T* __restrict__ out, int64_t ld_out) {
-  extern __shared__ float sm[];
-  const int hk = blockIdx.x, s = blockIdx.y;
-  const int len = pos0 + s + 1;
-  float* qs = sm;                      // [group][128]
-  float* sc = sm + group * 128;        // [group][len]
-  __shared__ float red[kAttnThreads / 32][kMaxGroup];
-  __shared__ float stat[2][kMaxGroup];  // max, 1/sum
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-
-  for (int i = tid; i < group * 128; i += kAttnThreads) {
-    const int h = i >> 7, d = i & 127;
-    qs[i] = DT<T>::to_f(q[(int64_t)(hk * group + h) * q_head_stride + (int64_t)s * 128 + d]);
-  }
-  __syncthreads();
-  const float scale = rsqrtf(128.0f);
-  const T* kh = kc + (int64_t)hk * chs;
-  const T* vh = vc + (int64_t)hk * chs;
-
-  // scores and per-thread maxima
-  float mx[kMaxGroup];
-#pragma unroll
-  for (int h = 0; h < kMaxGroup; ++h) mx[h] = -INFINITY;
-  for (int j = tid; j < len; j += kAttnThreads) {
-    float acc[kMaxGroup];
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.f;
-    const uint4* kr = reinterpret_cast<const uint4*>(kh + (int64_t)j * 128);
-#pragma unroll 4
-    for (int c = 0; c < 16; ++c) {
-      const uint4 raw = kr[c];
-      const T* e = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float kv = DT<T>::to_f(e[i]);
-#pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h)
-          if (h < group) acc[h] = fmaf(qs[h * 128 + c * 8 + i], kv, acc[h]);
-      }
-    }
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h)
-      if (h < group) {
-        const float t = round_to<T>(round_to<T>(acc[h]) * scale);
-        sc[h * len + j] = t;
-        mx[h] = fmaxf(mx[h], t);
-      }
-  }
-  // row maxima
-#pragma unroll
-  for (int h = 0; h < kMaxGroup; ++h) {
-    float v = mx[h];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if (lane == 0) red[warp][h] = v;
-  }
-  __syncthreads();
-  if (tid < group) {
-    float v = -INFINITY;
-    for (int w = 0; w < kAttnThreads / 32; ++w) v = fmaxf(v, red[w][tid]);
-    stat[0][tid] = v;
-  }
-  __syncthreads();
-  // exponentials (stored rounded) and their fp32 sum
-  float sum[kMaxGroup];
-#pragma unroll
-  for (int h = 0; h < kMaxGroup; ++h) sum[h] = 0.f;
-  for (int j = tid; j < len; j += kAttnThreads) {
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h)
-      if (h < group) {
-        const float e = expf(sc[h * len + j] - stat[0][h]);
-        sum[h] += e;
-        sc[h * len + j] = round_to<T>(e);
-      }
-  }
-#pragma unroll
-  for (int h = 0; h < kMaxGroup; ++h) {
-    float v = sum[h];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) red[warp][h] = v;
-  }
-  __syncthreads();
-  if (tid < group) {
-    float v = 0.f;
-    for (int w = 0; w < kAttnThreads / 32; ++w) v += red[w][tid];
-    stat[1][tid] = 1.0f / v;
-  }
-  __syncthreads();
-  for (int j = tid; j < len; j += kAttnThreads)
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h)
-      if (h < group) sc[h * len + j] = round_to<T>(sc[h * len + j] * stat[1][h]);
-  __syncthreads();
-
-  // out[h][d] = sum_j p[h][j] * V[j][d]: two halves of the block take even /
-  // odd j, 128 threads each cover d; halves are combined in a fixed order
-  const int half = tid >> 7, d = tid & 127;
-  float o[kMaxGroup];
-#pragma unroll
-  for (int h = 0; h < kMaxGroup; ++h) o[h] = 0.f;
-  for (int j = half; j < len; j += 2) {
-    const float v = DT<T>::to_f(vh[(int64_t)j * 128 + d]);
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h)
-      if (h < group) o[h] = fmaf(sc[h * len + j], v, o[h]);
-  }
-  __syncthreads();
-  float* comb = sm;  // reuse q area: [group][128] from the odd half
-  if (half == 1)
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h)
-      if (h < group) comb[h * 128 + d] = o[h];
-  __syncthreads();
-  if (half == 0) {
-    T* orow = out + (int64_t)s * ld_out + (int64_t)hk * group * 128;
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h)
-      if (h < group) orow[h * 128 + d] = DT<T>::from_f(o[h] + comb[h * 128 + d]);
-  }
-}
-
-}  // namespace
-}  // namespace ie
-
-extern "C" int ie_attention(ie_dtype dt, int S, int pos0, int n_q_heads, int n_kv_heads, int head_dim, const void* q,
-                            int64_t q_head_stride, const void* k_cache, const void* v_cache,
-                            int64_t cache_head_stride, void* out, int64_t ld_out, void* stream) {
-  using namespace ie;
-  if ((dt != IE_DTYPE_F16 && dt != IE_DTYPE_BF16) || S < 0 || pos0 < 0 || n_kv_heads <= 0 || n_q_heads <= 0)
-    return IE_ERR_INVALID_ARG;
-  if (head_dim != 128 || n_q_heads % n_kv_heads || n_q_heads / n_kv_heads > kMaxGroup) return IE_ERR_UNSUPPORTED;
-  if (S == 0) return IE_OK;
-  if (!q || !k_cache || !v_cache || !out) return IE_ERR_INVALID_ARG;
-  if (!aligned16(k_cache) || !aligned16(v_cache) || (cache_head_stride % 8)) return IE_ERR_ALIGNMENT;
-  if (ld_out < (int64_t)n_q_heads * 128 || q_head_stride < (int64_t)S * 128) return IE_ERR_INVALID_ARG;
-  if (cache_head_stride < (int64_t)(pos0 + S) * 128) return IE_ERR_INVALID_ARG;
-  const int group = n_q_heads / n_kv_heads;
-  const size_t smem = (size_t)group * (128 + (size_t)(pos0 + S)) * sizeof(float);
-  if (smem > 200 * 1024) return IE_ERR_UNSUPPORTED;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  dim3 grid(n_kv_heads, S);
-  cudaError_t e;
-  if (dt == IE_DTYPE_F16) {
-    auto k = attention_kernel<__half>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    k<<<grid, kAttnThreads, smem, st>>>(static_cast<const __half*>(q), q_head_stride,
-                                        static_cast<const __half*>(k_cache), static_cast<const __half*>(v_cache),
-                                        cache_head_stride, pos0, group, static_cast<__half*>(out), ld_out);
-  } else {
-    auto k = attention_kernel<__nv_bfloat16>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    k<<<grid, kAttnThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(q), q_head_stride,
-                                        static_cast<const __nv_bfloat16*>(k_cache),
-                                        static_cast<const __nv_bfloat16*>(v_cache), cache_head_stride, pos0, group,
-                                        static_cast<__nv_bfloat16*>(out), ld_out);
-  }
-  e = cudaGetLastError();
-  return e == cudaSuccess ? IE_OK : IE_ERR_LAUNCH;
-}
 
 // ------------------------------------------------ split-KV decode attention
 // Decode-time attention (a few query rows, each over its whole cache) spread
@@ -622,5 +454,295 @@ extern "C" int ie_attention_decode(ie_dtype dt, int R, int rows_per_seq, int n_q
   if (dt == IE_DTYPE_F16) { IE_FD(__half) }
   else { IE_FD(__nv_bfloat16) }
 #undef IE_FD
+  return e == cudaSuccess ? IE_OK : IE_ERR_LAUNCH;
+}
+
+// ------------------------------------------------------ prefill attention
+// Causal flash attention for many query rows of one sequence. CTA = 4 warps =
+// 64 query rows of one query head; each warp owns 16 rows and walks the key
+// blocks of 64 positions up to its causal limit:
+//   S = Q.K^T (m16n8k16, fp32) -> t = round(round(s) * rsqrt(128)) -> mask
+//   -> running max m, e = exp(t - m), p = round(e) -> O = O * exp(m_old - m)
+//   + p.V (m16n8k16) ; l = l * exp(m_old - m) + sum(e)
+// and writes round(O / l). Q, K and V tiles reach shared memory with 16-byte
+// cp.async copies into an XOR-swizzled layout (chunk c of row r at c ^ (r & 7))
+// so the ldmatrix fragment loads are conflict-free; K/V blocks are double
+// buffered. Query blocks are issued heaviest first (the causal work grows
+// with the block index). GQA: the K/V rows of head h / group.
+namespace ie {
+namespace {
+
+constexpr int kPaRows = 64, kPaKeys = 64, kPaThreads = 128;
+constexpr int kPaTile = 64 * 128 * 2;                  // one 64 x 128 tile, bytes
+constexpr int kPaSmem = kPaTile * 5;                   // Q + 2 x (K, V)
+
+struct PaParams {
+  const void* q;
+  int64_t q_head_stride;
+  const void* kc;
+  const void* vc;
+  int64_t chs;
+  int cache_rows, pos0, S, group;
+  void* out;
+  int64_t ld_out;
+};
+
+__device__ __forceinline__ uint32_t pa_swz(int r, int c) {  // byte offset of 16-B chunk c of tile row r
+  return (uint32_t)(r * 256 + ((c ^ (r & 7)) << 4));
+}
+__device__ __forceinline__ void cp16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c, uint32_t& d) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c, uint32_t& d) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+               : "r"(addr));
+}
+template <typename T>
+__device__ __forceinline__ void pa_mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __half>::value)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  T a = DT<T>::from_f(lo), b = DT<T>::from_f(hi);
+  return (uint32_t)(*reinterpret_cast<uint16_t*>(&a)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&b)) << 16);
+}
+
+// 64 rows x 128 dims starting at `src` (row stride 128 elements) into a
+// swizzled tile; rows >= valid_rows are zero-filled.
+template <typename T>
+__device__ __forceinline__ void load_tile(uint32_t dst, const T* src, int valid_rows) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int idx = threadIdx.x + i * kPaThreads;  // 0 .. 1023
+    const int r = idx >> 4, c = idx & 15;
+    const bool v = r < valid_rows;
+    cp16(dst + pa_swz(r, c), src + (int64_t)(v ? r : 0) * 128 + c * 8, v);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kPaThreads) prefill_attention_kernel(const PaParams p) {
+  extern __shared__ __align__(128) unsigned char pa_smem[];
+  const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(pa_smem));
+  // Q, then (K, V) of buffer 0, then (K, V) of buffer 1
+  const uint32_t sQ = sbase;
+  auto sK = [&](int b) { return sbase + (uint32_t)(1 + 2 * b) * kPaTile; };
+  auto sV = [&](int b) { return sbase + (uint32_t)(2 + 2 * b) * kPaTile; };
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  const int qb = gridDim.x - 1 - blockIdx.x, h = blockIdx.y, hk = h / p.group;
+  const int row0 = qb * kPaRows;
+  const int last_q = min(row0 + kPaRows, p.S) - 1;        // last real query row of the block
+  const int nkb = (p.pos0 + last_q) / kPaKeys + 1;         // key blocks the block needs
+  const T* qh = static_cast<const T*>(p.q) + (int64_t)h * p.q_head_stride + (int64_t)row0 * 128;
+  const T* kh = static_cast<const T*>(p.kc) + (int64_t)hk * p.chs;
+  const T* vh = static_cast<const T*>(p.vc) + (int64_t)hk * p.chs;
+
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  load_tile<T>(sQ, qh, p.S - row0);
+  load_tile<T>(sK(0), kh, p.cache_rows);
+  load_tile<T>(sV(0), vh, p.cache_rows);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+
+  const float scale = rsqrtf(128.0f);
+  const int qr0 = p.pos0 + row0 + warp * 16 + g;  // absolute positions of this lane's rows g and g+8
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[i][j] = 0.f;
+  uint32_t qf[8][4];
+
+  for (int kb = 0; kb < nkb; ++kb) {
+    const int buf = kb & 1;
+    if (kb + 1 < nkb) {
+      const int r = (kb + 1) * kPaKeys;
+      load_tile<T>(sK(buf ^ 1), kh + (int64_t)r * 128, p.cache_rows - r);
+      load_tile<T>(sV(buf ^ 1), vh + (int64_t)r * 128, p.cache_rows - r);
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    if (kb == 0) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int r = warp * 16 + (lane & 15), c = ks * 2 + (lane >> 4);
+        ldsm_x4(sQ + pa_swz(r, c), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+      }
+    }
+    // ---- S = Q K^T for 64 keys (8 n-tiles)
+    float s[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks)
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t b0, b1, b2, b3;
+        const int r = np * 16 + (lane & 7) + ((lane >> 4) << 3), c = ks * 2 + ((lane >> 3) & 1);
+        ldsm_x4(sK(buf) + pa_swz(r, c), b0, b1, b2, b3);
+        pa_mma<T>(s[2 * np], qf[ks], b0, b1);
+        pa_mma<T>(s[2 * np + 1], qf[ks], b2, b3);
+      }
+    // ---- scores, mask, running max
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int key = kb * kPaKeys + nt * 8 + 2 * t4 + (j & 1);
+        const int qpos = qr0 + ((j >> 1) << 3);
+        const float v = key <= qpos ? round_to<T>(round_to<T>(s[nt][j]) * scale) : -INFINITY;
+        s[nt][j] = v;
+        mx[j >> 1] = fmaxf(mx[j >> 1], v);
+      }
+    float corr[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      const float mn = fmaxf(m[r], mx[r]);
+      corr[r] = expf(m[r] - mn);  // 0 on the first block (m = -inf, mn finite)
+      m[r] = mn;
+      l[r] *= corr[r];
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      o[i][0] *= corr[0];
+      o[i][1] *= corr[0];
+      o[i][2] *= corr[1];
+      o[i][3] *= corr[1];
+    }
+    // ---- p = round(exp(t - m)); O += P V
+    uint32_t pf[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      float e[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        e[j] = expf(s[nt][j] - m[j >> 1]);
+        l[j >> 1] += e[j];
+      }
+      const int kk = nt >> 1, hi = nt & 1;
+      pf[kk][hi * 2 + 0] = pack2<T>(e[0], e[1]);
+      pf[kk][hi * 2 + 1] = pack2<T>(e[2], e[3]);
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+      for (int dp = 0; dp < 8; ++dp) {
+        uint32_t b0, b1, b2, b3;
+        const int r = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), c = dp * 2 + (lane >> 4);
+        ldsm_x4_t(sV(buf) + pa_swz(r, c), b0, b1, b2, b3);
+        pa_mma<T>(o[2 * dp], pf[kk], b0, b1);
+        pa_mma<T>(o[2 * dp + 1], pf[kk], b2, b3);
+      }
+    __syncthreads();  // the buffer is refilled two blocks later
+  }
+  // ---- normalise and store
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    l[r] += __shfl_xor_sync(0xffffffffu, l[r], 1);
+    l[r] += __shfl_xor_sync(0xffffffffu, l[r], 2);
+  }
+  const float inv[2] = {1.0f / l[0], 1.0f / l[1]};
+  T* out = static_cast<T*>(p.out);
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = row0 + warp * 16 + g + 8 * r;
+    if (row >= p.S) continue;
+    T* orow = out + (int64_t)row * p.ld_out + (int64_t)h * 128;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      const uint32_t v = pack2<T>(o[nt][2 * r] * inv[r], o[nt][2 * r + 1] * inv[r]);
+      *reinterpret_cast<uint32_t*>(orow + nt * 8 + 2 * t4) = v;
+    }
+  }
+}
+
+template <typename T>
+cudaError_t launch_prefill_attention(const PaParams& p, int n_q_heads, cudaStream_t st) {
+  auto kernel = prefill_attention_kernel<T>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPaSmem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.S + kPaRows - 1) / kPaRows, n_q_heads);
+  cfg.blockDim = dim3(kPaThreads);
+  cfg.dynamicSmemBytes = kPaSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  const char* env = getenv("IE_PDL");
+  cfg.numAttrs = (env && env[0] == '0') ? 0 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
+}  // namespace
+}  // namespace ie
+
+extern "C" int ie_attention(ie_dtype dt, int S, int pos0, int n_q_heads, int n_kv_heads, int head_dim, const void* q,
+                            int64_t q_head_stride, const void* k_cache, const void* v_cache,
+                            int64_t cache_head_stride, void* out, int64_t ld_out, void* stream) {
+  using namespace ie;
+  if ((dt != IE_DTYPE_F16 && dt != IE_DTYPE_BF16) || S < 0 || pos0 < 0 || n_kv_heads <= 0 || n_q_heads <= 0)
+    return IE_ERR_INVALID_ARG;
+  if (head_dim != 128 || n_q_heads % n_kv_heads) return IE_ERR_UNSUPPORTED;
+  if (S == 0) return IE_OK;
+  if (!q || !k_cache || !v_cache || !out) return IE_ERR_INVALID_ARG;
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out) || (cache_head_stride % 8) ||
+      (q_head_stride % 8) || (ld_out % 8))
+    return IE_ERR_ALIGNMENT;
+  if (ld_out < (int64_t)n_q_heads * 128 || q_head_stride < (int64_t)S * 128) return IE_ERR_INVALID_ARG;
+  if (cache_head_stride < (int64_t)(pos0 + S) * 128) return IE_ERR_INVALID_ARG;
+  if (S <= 16)  // few rows: the split-KV kernel (exact chain)
+    return ie_attention_decode(dt, S, S, n_q_heads, n_kv_heads, head_dim, q, q_head_stride, k_cache, v_cache,
+                               cache_head_stride, 0, pos0 + S, nullptr, pos0, out, ld_out, stream);
+  if ((int64_t)S > 65535LL * kPaRows || n_q_heads > 65535) return IE_ERR_UNSUPPORTED;
+  PaParams p;
+  p.q = q;
+  p.q_head_stride = q_head_stride;
+  p.kc = k_cache;
+  p.vc = v_cache;
+  p.chs = cache_head_stride;
+  const int64_t rows = cache_head_stride / 128;
+  p.cache_rows = rows > INT_MAX ? INT_MAX : (int)rows;
+  p.pos0 = pos0;
+  p.S = S;
+  p.group = n_q_heads / n_kv_heads;
+  p.out = out;
+  p.ld_out = ld_out;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const cudaError_t e = dt == IE_DTYPE_F16 ? launch_prefill_attention<__half>(p, n_q_heads, st)
+                                           : launch_prefill_attention<__nv_bfloat16>(p, n_q_heads, st);
   return e == cudaSuccess ? IE_OK : IE_ERR_LAUNCH;
 }

@@ -5,6 +5,7 @@
 #include "skinny.cuh"
 #include "gemm_tc.cuh"
 #include "attention.cuh"
+#include "norm.cuh"
 
 using namespace ie;
 
@@ -58,7 +59,8 @@ int ie_device_status(int clear) {
   const int a = read_tc_status(clear != 0);
   const int b = read_skinny_status(clear != 0);
   const int c = read_attn_status(clear != 0);
-  return a != IE_OK ? a : (b != IE_OK ? b : c);
+  const int d = read_norm_status(clear != 0);
+  return a != IE_OK ? a : (b != IE_OK ? b : (c != IE_OK ? c : d));
 }
 
 static int gemm_store(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw,

@@ -19,6 +19,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <algorithm>
+#include <chrono>
 #include <cstdint>
 #include <cstdio>
 #include <vector>
@@ -105,13 +106,44 @@ REF_API void model_free() {
   g_w = ModelWeights{};
 }
 
+// Device pointers of the current weights, for running another engine on the
+// same model: out[0..4] = embedding, final norm, lm_head, rope cos, rope sin;
+// then per layer input_layernorm, w_q, w_k, w_v, w_o, post_attention_layernorm,
+// w_gate, w_up, w_down. n: capacity of out. Returns the count written.
+REF_API int model_weight_ptrs(void** out, int n) {
+  const int need = 5 + 9 * NUM_LAYERS;
+  if (n < need) return -1;
+  out[0] = g_w.emb_lookup; out[1] = g_w.final_norm; out[2] = g_w.lm_head;
+  out[3] = g_w.rope.cos; out[4] = g_w.rope.sin;
+  for (int l = 0; l < NUM_LAYERS; ++l) {
+    const Layer& L = g_w.layers[l];
+    void** o = out + 5 + 9 * l;
+    o[0] = L.input_layernorm; o[1] = L.transformer.w_q; o[2] = L.transformer.w_k; o[3] = L.transformer.w_v;
+    o[4] = L.transformer.w_o; o[5] = L.post_attention_layernorm; o[6] = L.ffn_block.w_gate;
+    o[7] = L.ffn_block.w_up; o[8] = L.ffn_block.w_down;
+  }
+  return need;
+}
+
 // Prefill the prompt, then n_new - 1 decode steps (n_new tokens in total).
 // forced (nullable, n_new entries): the token appended after step i is
 // forced[i] instead of the model's own pick (teacher forcing); out_tokens[i]
 // is always the model's pick. out_margin[i] (nullable): top-1 minus top-2
 // logit of step i (fp16 logits read back).
+REF_API int model_generate_timed(const int* prompt, int n_prompt, int n_new, const int* forced, int* out_tokens,
+                                 float* out_margin, double* prefill_ms, double* decode_ms);
+
 REF_API int model_generate(const int* prompt, int n_prompt, int n_new, const int* forced, int* out_tokens,
                            float* out_margin) {
+  return model_generate_timed(prompt, n_prompt, n_new, forced, out_tokens, out_margin, nullptr, nullptr);
+}
+
+// As model_generate; prefill_ms / decode_ms (nullable) receive the host wall
+// time of the prefill call and of the n_new - 1 decode_step calls (each of
+// which ends in the reference's blocking copy of the token, decode.cu:47).
+// With out_margin set the margin read-backs fall inside the decode time.
+REF_API int model_generate_timed(const int* prompt, int n_prompt, int n_new, const int* forced, int* out_tokens,
+                                 float* out_margin, double* prefill_ms, double* decode_ms) {
   int* tokenid_buff;
   half *data_buffer, *aux_buffer, *attn_buffer, *output_distr;
   int* output_token;
@@ -138,9 +170,12 @@ REF_API int model_generate(const int* prompt, int n_prompt, int n_new, const int
     return a - b;
   };
   int seq_len = n_prompt;
+  cudaDeviceSynchronize();
+  const auto t0 = std::chrono::steady_clock::now();
   cudaMemcpy(tokenid_buff, prompt, n_prompt * sizeof(int), cudaMemcpyHostToDevice);
   int tok = prefill(handle, g_w, seq_len, tokenid_buff, data_buffer, aux_buffer, attn_buffer, output_distr,
                     output_token, workspace, kv_cache);
+  const auto t1 = std::chrono::steady_clock::now();
   for (int i = 0; i < n_new; ++i) {
     out_tokens[i] = tok;
     if (out_margin) out_margin[i] = margin();
@@ -152,6 +187,9 @@ REF_API int model_generate(const int* prompt, int n_prompt, int n_new, const int
                       output_token, workspace, kv_cache);
   }
   const cudaError_t e = cudaDeviceSynchronize();
+  const auto t2 = std::chrono::steady_clock::now();
+  if (prefill_ms) *prefill_ms = std::chrono::duration<double, std::milli>(t1 - t0).count();
+  if (decode_ms) *decode_ms = std::chrono::duration<double, std::milli>(t2 - t1).count();
   cudaFree(workspace); cudaFree(kv_cache); cudaFree(data_buffer); cudaFree(aux_buffer); cudaFree(attn_buffer);
   cudaFree(output_distr); cudaFree(output_token); cudaFree(tokenid_buff);
   cublasDestroy(handle);

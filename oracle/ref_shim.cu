@@ -17,6 +17,9 @@
 #include "kernels/sampling.cuh"
 #include "kernels/multiply_by_weight.cuh"
 #include "kernels/rope.cuh"
+#include "kernels/rmsnorm.cuh"
+#include "kernels/residual_add.cuh"
+#include "kernels/emblookup.cuh"
 
 // non-static helpers of kernels/attn.cu:12 and :265
 void multiply_kqv_proj(cublasHandle_t handle, const half* d_W, const half* d_input, half* d_out, const int seq_len,
@@ -88,4 +91,17 @@ REF_API int ref_init_rope_buffer(float** cos, float** sin) {
 
 REF_API void ref_o_proj(int seq_len, const void* d_pre_proj, const void* w_o, void* d_out) {
   multiply_preproj_Wo(handle(), seq_len, (const half*)d_pre_proj, (const half*)w_o, (half*)d_out);
+}
+
+// The kernels a decode step runs between the projections (decode.cu:14-44).
+REF_API void ref_rmsnorm(int seq_len, void* d_input, void* d_weight, void* d_output) {
+  rmsnorm(seq_len, (half*)d_input, (half*)d_weight, (half*)d_output);
+}
+
+REF_API void ref_residual_add(int rows, int cols, void* d_x, void* d_delta) {
+  residual_add(rows, cols, (half*)d_x, (half*)d_delta);
+}
+
+REF_API void ref_emblookup(int seq_len, int* d_tokens, void* d_table, void* d_output) {
+  emblookup(seq_len, d_tokens, (half*)d_table, (half*)d_output);
 }

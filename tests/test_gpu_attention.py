@@ -10,8 +10,11 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 @pytest.mark.parametrize("S,pos0,nq,nkv", [(1, 0, 32, 8), (1, 300, 32, 8), (37, 0, 32, 8), (16, 50, 8, 2),
-                                           (5, 2043, 4, 1)])
+                                           (5, 2043, 4, 1), (17, 0, 8, 2), (64, 0, 8, 2), (65, 3, 8, 2),
+                                           (300, 100, 32, 8), (1024, 0, 8, 2)])
 def test_attention_core(ie, cuda, dt, S, pos0, nq, nkv):
+    """S <= 16: split-KV kernel; S > 16: tensor-core flash kernel (chunked
+    prefill when pos0 > 0; ragged last query and key blocks)."""
     ctx = 2048 + 64
     rng = np.random.default_rng(S * 1000 + pos0 + nq)
     q = oracle.round_dt(rng.standard_normal((nq, S, 128), dtype=np.float32), dt)
