@@ -33,8 +33,11 @@
 // over the GPU: one thread-block cluster of kFdCluster CTAs per (query row,
 // KV head); CTA c of the cluster takes cache rows [c*len/8, (c+1)*len/8).
 //  * Cache rows reach shared memory by untiled bulk copies
-//    (cp.async.bulk, 64 rows = 16 KB each) through a 4-deep ring completed on
-//    mbarriers, so a CTA keeps up to 64 KB of K/V in flight.
+//    (cp.async.bulk, 64 rows = 16 KB each) through a 6-deep ring completed on
+//    mbarriers, so a CTA keeps up to 96 KB of K/V in flight. Rows older than
+//    the launch's first query row are requested before the kernel waits for
+//    its predecessor (programmatic launch), so their latency overlaps the
+//    QKV projection's tail.
 //  * The softmax keeps the reference's chain (scores rounded, scaled and
 //    rounded; e = exp(t - max) summed in fp32 and stored rounded;
 //    p = round(round(e) * (1/sum))): the row maximum and the sum are exact
@@ -56,7 +59,7 @@ constexpr int kFdCluster = 8;
 constexpr int kFdThreads = 256;
 constexpr int kFdWarps = kFdThreads / 32;
 constexpr int kFdRows = 64;
-constexpr int kFdStages = 4;
+constexpr int kFdStages = 6;
 constexpr int kFdRingBytes = kFdStages * kFdRows * 128 * 2;
 constexpr unsigned long long kFdWaitNs = 2000000000ull;
 
@@ -158,19 +161,13 @@ __global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
   const int hk = blockIdx.y, m = blockIdx.z;
 
-  if (tid == 0) {
-    for (int s = 0; s < kFdStages; ++s)
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(fd_smem_u32(&bars[s])) : "memory");
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    abort_s = 0;
-    fail_at = INT_MAX;
-  }
-  // q and the cache rows come from the previous kernel (programmatic launch)
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  __syncthreads();
-
+  // The cache rows before the first query row of this row's sequence were
+  // written by earlier launches; the preceding kernel (the QKV projection)
+  // writes only rows from there on, and q. So the copies of the older rows
+  // are issued before waiting for that kernel, the rest after it.
   const int pos = p.positions ? p.positions[m] : p.pos0 + m;
+  const int m_first = m - m % p.rows_per_seq;
+  const int first_new = p.positions ? p.positions[m_first] : p.pos0 + m_first;
   const bool bad = pos < 0 || pos >= p.cache_rows;
   if (bad && rank == 0 && tid == 0) atomicExch(&g_attn_status, IE_ERR_INVALID_ARG);
   const int len = bad ? 0 : pos + 1;
@@ -182,22 +179,56 @@ __global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
   const T* vh = static_cast<const T*>(p.vc) + base;
 
   int issued = 0;  // thread 0 only
-  auto issue = [&](int i) {
-    const int slot = i % kFdStages, c = i < nk ? i : i - nk;
-    const int r0 = j0 + c * kFdRows;
-    const int rows = min(kFdRows, j0 + n - r0);
-    const uint32_t bytes = (uint32_t)rows * 128u * sizeof(T);
-    const T* src = (i < nk ? kh : vh) + (int64_t)r0 * 128;
-    const uint32_t bar = fd_smem_u32(&bars[slot]);
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     fd_smem_u32(ring + slot * kFdRows * 128)),
-                 "l"(src), "r"(bytes), "r"(bar)
+  auto chunk_of = [&](int i, int& r0, int& rows) {
+    const int c = i < nk ? i : i - nk;
+    r0 = j0 + c * kFdRows;
+    rows = min(kFdRows, j0 + n - r0);
+  };
+  // expect the whole chunk on its slot's barrier
+  auto arm = [&](int i) {
+    int r0, rows;
+    chunk_of(i, r0, rows);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(fd_smem_u32(&bars[i % kFdStages])),
+                 "r"((uint32_t)rows * 128u * (uint32_t)sizeof(T))
                  : "memory");
     issued = i + 1;
   };
+  // copy cache rows [lo, hi) (absolute) of chunk i into its slot
+  auto copy = [&](int i, int lo, int hi) {
+    int r0, rows;
+    chunk_of(i, r0, rows);
+    lo = max(lo, r0);
+    hi = min(hi, r0 + rows);
+    if (hi <= lo) return;
+    const int slot = i % kFdStages;
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     fd_smem_u32(ring + (slot * kFdRows + (lo - r0)) * 128)),
+                 "l"((i < nk ? kh : vh) + (int64_t)lo * 128), "r"((uint32_t)(hi - lo) * 128u * (uint32_t)sizeof(T)),
+                 "r"(fd_smem_u32(&bars[slot]))
+                 : "memory");
+  };
+  auto issue = [&](int i) {
+    arm(i);
+    copy(i, 0, INT_MAX);
+  };
+
+  const int first = min(kFdStages, total);
+  if (tid == 0) {
+    for (int s = 0; s < kFdStages; ++s)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(fd_smem_u32(&bars[s])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    abort_s = 0;
+    fail_at = INT_MAX;
+    for (int i = 0; i < first; ++i) {
+      arm(i);
+      copy(i, 0, first_new);
+    }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid == 0)
-    for (int i = 0; i < min(kFdStages, total); ++i) issue(i);
+    for (int i = 0; i < first; ++i) copy(i, first_new, INT_MAX);
+  __syncthreads();
 
   for (int i = tid; i < G * 128; i += kFdThreads) {
     const int h = i >> 7, d = i & 127;
@@ -225,21 +256,35 @@ __global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
     wait_chunk(i);
     const T* tile = ring + (i % kFdStages) * kFdRows * 128;
     const int r0 = i * kFdRows, rows = min(kFdRows, n - r0);
-    for (int r = warp; r < rows; r += kFdWarps) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(tile + r * 128 + lane * 4);
-      const T* e = reinterpret_cast<const T*>(&raw);
-      float s[G];
+    // four rows per warp at a time: independent loads and shuffle chains
+    for (int rb = warp; rb < rows; rb += 4 * kFdWarps) {
+      uint2 raw[4];
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        float a = qr[h][0] * DT<T>::to_f(e[0]);
-#pragma unroll
-        for (int d = 1; d < 4; ++d) a = fmaf(qr[h][d], DT<T>::to_f(e[d]), a);
-        s[h] = a;
+      for (int u = 0; u < 4; ++u) {
+        const int r = rb + u * kFdWarps;
+        raw[u] = r < rows ? *reinterpret_cast<const uint2*>(tile + r * 128 + lane * 4) : make_uint2(0, 0);
       }
-      const float v = warp_sum_transposed<G>(s, lane);
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const T* e = reinterpret_cast<const T*>(&raw[u]);
+        float s[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          float a = qr[h][0] * DT<T>::to_f(e[0]);
+#pragma unroll
+          for (int d = 1; d < 4; ++d) a = fmaf(qr[h][d], DT<T>::to_f(e[d]), a);
+          s[h] = a;
+        }
+        v[u] = warp_sum_transposed<G>(s, lane);
+      }
       if ((lane & (32 / G - 1)) == 0) {
         const int h = lane / (32 / G);
-        sc[h * p.cap + r0 + r] = DT<T>::from_f(round_to<T>(round_to<T>(v) * scale));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int r = rb + u * kFdWarps;
+          if (r < rows) sc[h * p.cap + r0 + r] = DT<T>::from_f(round_to<T>(round_to<T>(v[u]) * scale));
+        }
       }
     }
     next(i);
@@ -318,6 +363,7 @@ __global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
     wait_chunk(i);
     const T* tile = ring + (i % kFdStages) * kFdRows * 128;
     const int r0 = (i - nk) * kFdRows, rows = min(kFdRows, n - r0);
+#pragma unroll 4
     for (int r = warp; r < rows; r += kFdWarps) {
       const uint2 raw = *reinterpret_cast<const uint2*>(tile + r * 128 + lane * 4);
       const T* e = reinterpret_cast<const T*>(&raw);

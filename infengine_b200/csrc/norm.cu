@@ -12,6 +12,9 @@
 // per row holds four virtual threads per thread and runs the same tree (the
 // first two levels in registers, the next three in shared memory, the last
 // five as shuffles), so its sums are identical to the reference's.
+// (Fusing this into the prologue of the consuming projection was measured
+// slower: every CTA of every wave then re-reads the row through an L2 that is
+// saturated by the weight stream.)
 #include "ie_common.cuh"
 #include "norm.cuh"
 
@@ -24,21 +27,43 @@ namespace {
 constexpr int kNormThreads = 256;
 constexpr int kVirtual = 1024;  // the reference's block size
 
+constexpr int kNormMaxChunks = 8;  // 16-byte chunks per thread: H <= 256 * 8 * 8
+
+// One CTA per row. The weight chunks are requested before waiting for the
+// previous kernel (they are never written by it); the row is read once with
+// 16-byte loads, kept in registers for the output and staged in shared memory
+// for the sums, which then follow the reference's per-virtual-thread order.
 template <typename T>
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const T* x, int64_t ldx,
-                                                               const T* __restrict__ w, T* out, int64_t ldo, int H,
-                                                               float eps) {
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const T* x, int64_t ldx, const T* __restrict__ w,
+                                                               T* out, int64_t ldo, int H, float eps) {
+  extern __shared__ __align__(16) unsigned char norm_smem[];
   __shared__ float s[kNormThreads];
+  T* xs = reinterpret_cast<T*>(norm_smem);
+  const int row = blockIdx.x, t = threadIdx.x, nv = H / 8;
+  uint4 wv[kNormMaxChunks], xv[kNormMaxChunks];
+#pragma unroll
+  for (int k = 0; k < kNormMaxChunks; ++k) {
+    const int c = t + k * kNormThreads;
+    if (c < nv) wv[k] = ld_act_v4(w + 8 * c);
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const int row = blockIdx.x, t = threadIdx.x;
   const T* xr = x + (int64_t)row * ldx;
+#pragma unroll
+  for (int k = 0; k < kNormMaxChunks; ++k) {
+    const int c = t + k * kNormThreads;
+    if (c < nv) {
+      xv[k] = ld_act_v4(xr + 8 * c);
+      *reinterpret_cast<uint4*>(xs + 8 * c) = xv[k];
+    }
+  }
+  __syncthreads();
   float v[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     float a = 0.f;
     for (int i = t + k * kNormThreads; i < H; i += kVirtual) {
-      const float d = DT<T>::to_f(xr[i]);
+      const float d = DT<T>::to_f(xs[i]);
       a += d * d;
     }
     v[k] = a;  // virtual thread t + 256 k
@@ -61,8 +86,19 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const T* x, int64
   __syncthreads();
   const float scale = rsqrtf(s[0] / (float)H + eps);
   T* orow = out + (int64_t)row * ldo;
-  for (int i = t; i < H; i += kNormThreads)
-    orow[i] = DT<T>::from_f(round_to<T>(DT<T>::to_f(xr[i]) * scale) * DT<T>::to_f(w[i]));
+#pragma unroll
+  for (int k = 0; k < kNormMaxChunks; ++k) {
+    const int c = t + k * kNormThreads;
+    if (c < nv) {
+      const T* xe = reinterpret_cast<const T*>(&xv[k]);
+      const T* we = reinterpret_cast<const T*>(&wv[k]);
+      uint4 ov;
+      T* oe = reinterpret_cast<T*>(&ov);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) oe[i] = DT<T>::from_f(round_to<T>(DT<T>::to_f(xe[i]) * scale) * DT<T>::to_f(we[i]));
+      *reinterpret_cast<uint4*>(orow + 8 * c) = ov;
+    }
+  }
 }
 
 // out[m] = table[tokens[m]]; a token outside [0, vocab) gives a zero row and
@@ -96,10 +132,11 @@ __global__ void advance_kernel(int B, const int* tokens, int* positions, int* hi
 }
 
 template <typename K, typename... Args>
-cudaError_t launch(K kernel, dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+cudaError_t launch(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -121,7 +158,7 @@ bool pdl_launch_enabled() {
 
 cudaError_t launch_advance(int B, const int* tokens, int* positions, int* history, int slots, int* step,
                            cudaStream_t st) {
-  return launch(advance_kernel, dim3(1), dim3(256), st, B, tokens, positions, history, slots, step);
+  return launch(advance_kernel, dim3(1), dim3(256), 0, st, B, tokens, positions, history, slots, step);
 }
 
 int read_norm_status(bool clear) {
@@ -142,15 +179,19 @@ extern "C" int ie_rmsnorm(ie_dtype dt, int M, int H, const void* x, int64_t ldx,
                           int64_t ldo, float eps, void* stream) {
   if ((dt != IE_DTYPE_F16 && dt != IE_DTYPE_BF16) || M < 0 || H <= 0) return IE_ERR_INVALID_ARG;
   if (M == 0) return IE_OK;
-  if (!x || !w || !out || ldx < H || ldo < H || M > 2147483647) return IE_ERR_INVALID_ARG;
+  if (!x || !w || !out || ldx < H || ldo < H) return IE_ERR_INVALID_ARG;
+  if (H % 8 || ldx % 8 || ldo % 8 || !aligned16(x) || !aligned16(w) || !aligned16(out)) return IE_ERR_ALIGNMENT;
+  if (H > kNormThreads * kNormMaxChunks * 8) return IE_ERR_UNSUPPORTED;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const size_t smem = (size_t)H * 2;
   cudaError_t e;
   if (dt == IE_DTYPE_F16)
-    e = launch(rmsnorm_kernel<__half>, dim3(M), dim3(kNormThreads), st, static_cast<const __half*>(x), ldx,
+    e = launch(rmsnorm_kernel<__half>, dim3(M), dim3(kNormThreads), smem, st, static_cast<const __half*>(x), ldx,
                static_cast<const __half*>(w), static_cast<__half*>(out), ldo, H, eps);
   else
-    e = launch(rmsnorm_kernel<__nv_bfloat16>, dim3(M), dim3(kNormThreads), st, static_cast<const __nv_bfloat16*>(x),
-               ldx, static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(out), ldo, H, eps);
+    e = launch(rmsnorm_kernel<__nv_bfloat16>, dim3(M), dim3(kNormThreads), smem, st,
+               static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w),
+               static_cast<__nv_bfloat16*>(out), ldo, H, eps);
   return e == cudaSuccess ? IE_OK : IE_ERR_LAUNCH;
 }
 
@@ -163,10 +204,10 @@ extern "C" int ie_embed(ie_dtype dt, int M, int H, int vocab, const int* tokens,
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (dt == IE_DTYPE_F16)
-    e = launch(embed_kernel<__half>, dim3(M), dim3(256), st, tokens, static_cast<const __half*>(table), vocab, H,
+    e = launch(embed_kernel<__half>, dim3(M), dim3(256), 0, st, tokens, static_cast<const __half*>(table), vocab, H,
                static_cast<__half*>(out), ldo);
   else
-    e = launch(embed_kernel<__nv_bfloat16>, dim3(M), dim3(256), st, tokens,
+    e = launch(embed_kernel<__nv_bfloat16>, dim3(M), dim3(256), 0, st, tokens,
                static_cast<const __nv_bfloat16*>(table), vocab, H, static_cast<__nv_bfloat16*>(out), ldo);
   return e == cudaSuccess ? IE_OK : IE_ERR_LAUNCH;
 }
