@@ -1,30 +1,39 @@
 #!/usr/bin/env python
-"""Benchmark of the infengine weight-matmul hot path on B200.
+"""Benchmark of infengine's decode on B200 (bs=1).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-One step = one bs=1 decode token through the weight-matmul path of
-random-init Llama-3.1-8B (bf16, N(0,0.02) weights, fixed seed):
-    32 x [ fused Q/K/V projection + RoPE into the KV cache (position 2047),
-           O projection, FFN gate/up + SwiGLU, FFN down ]
-    + lm_head with the fused greedy argmax.
-15.01 GB of weights are streamed per step (far above the 126 MB L2, so no
-flush is needed). The attention core, RMSNorm and residual adds are not part
-of this path and are not run: every layer's projections read the step's
-hidden state and the O projection reads the Q output as its stand-in for the
-attention output.
+One step = one greedy decode token of random-init Llama-3.1-8B (bf16,
+N(0,0.02) weights from a fixed seed, RMSNorm weights 1) right after a
+2048-token prompt: embedding, 32 x [RMSNorm, fused QKV+RoPE into the KV
+cache, split-KV attention, O projection + residual, RMSNorm, FFN gate/up +
+SwiGLU, FFN down + residual], final RMSNorm, lm_head + greedy argmax. Our arm
+runs it through the decode engine (ie_engine_decode: one CUDA graph per step,
+the id kept on the device); 15.01 GB of weights are streamed per step (far
+above the 126 MB L2, so no flush is needed). `value` is device-timed tok/s;
+`e2e` is the same through ie_engine_step with the token copied in from and
+the id copied out to the host every step.
 
-Our arm captures the step (129 kernel launches through the C-ABI) in one CUDA
-graph. The reference arm (--impl reference) runs the reference's own code
-for the same path, compiled from its sources for sm_100a (cuBLAS GEMMs,
-its RoPE, SwiGLU and argmax kernels; fp16, the reference's only dtype),
-launched eagerly on the legacy default stream as its decode loop does.
+Also reported: the weight-matmul path alone (`matmul_path`: the projections
+and lm_head without attention, norms or residuals, one graph of 129 launches;
+the north star's >= 80 % of HBM target) with the `roofline` of its dominant
+kernel (FFN gate/up + SwiGLU); BASELINE configs 1-4 one by one (`configs`);
+the M=2048 prefill projection chain against the sustained bf16 peak
+(`prefill`); batch-8 decode and the M=5 verify pass through the engine; the
+CPU golden of the path (`cpu_baseline`).
+
+The reference arm (--impl reference) runs the reference's own decode loop
+(prefill.cu / decode.cu with its kernels and cuBLAS, built from its sources
+for sm_100a by oracle/Makefile; fp16, its only dtype) on random-init weights:
+decode_step per token, eager on the legacy default stream, each step ending
+in its blocking copy of the token to the host.
 
 For N > 1 (torchrun) the same token stream is split by tensor parallelism
-(infengine_b200.tp: Q/K/V and gate/up column-split, O and down row-split with
-an fp32 NCCL allreduce, lm_head vocabulary-split with a max over packed argmax
-keys); the value is tok/s of the one stream (strong scaling), timed as the
-max over ranks.
+(one engine per rank: Q/K/V and gate/up column-split, O and down row-split
+and reduced over NVLink with the residual add fused, lm_head
+vocabulary-split with a max over packed argmax keys); the value is tok/s of
+the one stream (strong scaling), timed as the max over ranks. The reference
+arm has one GPU: rank 0 runs it, the other ranks exit.
 """
 from __future__ import annotations
 
@@ -46,6 +55,7 @@ METRIC = "decode tok/s bs1 & matmul HBM GB/s, prefill GEMM TFLOPS vs B200 roofli
 H, F, V, L = 4096, 14336, 128256, 32
 NQ, NKV, HD, CTX = 32, 8, 128, 8192
 POS = 2047  # the 2048th token: decode right after a 2048-token prompt
+PROMPT = 2048
 LAYER_WEIGHT_ELEMS = (NQ + 2 * NKV) * HD * H + H * H + 3 * F * H
 WEIGHT_BYTES = 2 * (L * LAYER_WEIGHT_ELEMS + V * H)
 GATE_UP_BYTES = 2 * (2 * F * H + H + F)  # one gate/up+SwiGLU launch at M=1
@@ -194,6 +204,9 @@ class OursStep:
         self.ap = torch.empty(S, H, device=dev, dtype=torch.bfloat16)
         self.hp = torch.empty(S, F, device=dev, dtype=torch.bfloat16)
         self.op = torch.empty(S, H, device=dev, dtype=torch.bfloat16)
+
+    def release_prefill(self):
+        self.xp = self.qp = self.ap = self.hp = self.op = None
 
     def prefill(self):
         """32 x [fused QKV+RoPE, O, gate/up+SwiGLU, down] at M = S tokens (positions 0..S-1)."""
@@ -504,7 +517,83 @@ def single_case(torch, name: str, steps: int, seed: int):
     print(json.dumps({"case": name, "launches": steps}))
 
 
+# ------------------------------------------------ full model through the engine
+def full_model_weights(torch, dev, seed, layers, lm):
+    """Engine weights of the random-init model: the projection weights of
+    make_weights (or their tensor-parallel shards), a seeded N(0,0.02)
+    embedding table, RMSNorm weights of 1 (the HF initialisation) and the
+    Llama-3.1 RoPE tables."""
+    from infengine_b200.host import rope_tables
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed + 2)
+    emb = torch.randn(V, H, generator=g, device=dev, dtype=torch.float32).mul_(0.02).to(torch.bfloat16)
+    ones = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    cos, sin = (torch.from_numpy(t).to(dev) for t in rope_tables(CTX))
+    return dict(embedding=emb, final_norm=ones, lm_head=lm, rope_cos=cos, rope_sin=sin,
+                layers=[dict(attn_norm=ones, wq=w["wq"], wk=w["wk"], wv=w["wv"], wo=w["wo"], ffn_norm=ones,
+                             w_gate=w["wg"], w_up=w["wu"], w_down=w["wd"]) for w in layers])
+
+
+def make_engine(weights, world, rank, batch, ctx, comm=None, exchange=None, plan=None):
+    from infengine_b200.engine import LlamaEngine
+    dims = dict(n_layers=L, hidden=H, n_q_heads=NQ // world, n_kv_heads=NKV // world, head_dim=HD,
+                ffn_dim=F // world, vocab=V, rms_eps=1e-5)
+    tp = None
+    if world > 1:
+        vs = plan.vocab_slice()
+        tp = dict(world=world, rank=rank, comm=comm, exchange=exchange, lm_rows=vs.stop - vs.start,
+                  lm_offset=vs.start)
+    return LlamaEngine(weights, dims, dtype="bf16", max_batch=batch, max_ctx=ctx, max_prefill=PROMPT, tp=tp)
+
+
+def prompts(seed, n):
+    return np.random.default_rng(seed + 3).integers(0, V, size=(n, PROMPT)).astype(np.int32)
+
+
+def reference_decode(seed, steps, warmup):
+    """The reference's own decode loop (prefill.cu / decode.cu with its
+    kernels, built from its sources by oracle/Makefile) on random-init fp16
+    weights: tok/s of `steps` decode steps after a PROMPT-token prompt."""
+    import ctypes
+    R = ctypes.CDLL(str(ROOT / "oracle" / "_ref" / "libref_model_ref.so"))
+    R.model_init.argtypes = [ctypes.c_ulonglong]
+    dbl = ctypes.POINTER(ctypes.c_double)
+    R.model_generate_timed.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                       ctypes.c_void_p, ctypes.c_void_p, dbl, dbl]
+    assert R.model_init(seed) == 0
+    prompt = prompts(seed, 1)[0]
+    pm, dm = ctypes.c_double(), ctypes.c_double()
+    out = np.zeros(steps + 1, np.int32)
+    vp = ctypes.c_void_p
+    assert R.model_generate_timed(prompt.ctypes.data_as(vp), PROMPT, warmup + 1, None, out.ctypes.data_as(vp), None,
+                                  ctypes.byref(pm), ctypes.byref(dm)) == 0
+    assert R.model_generate_timed(prompt.ctypes.data_as(vp), PROMPT, steps + 1, None, out.ctypes.data_as(vp), None,
+                                  ctypes.byref(pm), ctypes.byref(dm)) == 0
+    R.model_free()
+    return {"decode_ms": dm.value, "prefill_ms": pm.value, "tokens": out}
+
+
 # ------------------------------------------------------------------- main
+def timed(torch, stream, fn, world, dev):
+    """Device time (ms) of fn() on `stream`, max over ranks."""
+    import torch.distributed as dist
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    fn()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -529,145 +618,179 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:  # the reference runs on one GPU; other ranks have no work
+            return
+        world = 1
     if world > 1:
         from datetime import timedelta
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-
-    if args.impl == "reference" and rank != 0:
-        dist.destroy_process_group() if world > 1 else None
-        return
-
-    def barrier():
-        if world > 1 and args.impl == "ours":
-            dist.barrier()
-
     hbm_peak, tf_peak, tf_peak_sus, peak_src = load_peaks()
-    stream = torch.cuda.Stream(device=dev)
-    if args.impl == "ours" and world > 1:
-        step = TPStep(torch, dev, args.seed, world, rank)
-    else:
-        step = (OursStep if args.impl == "ours" else RefStep)(torch, dev, args.seed)
-    torch.cuda.synchronize()
+    if args.impl == "reference":
+        run_reference(torch, dev, args)
+        return
+    run_ours(torch, dist, dev, args, world, rank, local, hbm_peak, tf_peak, tf_peak_sus, peak_src)
 
-    graph = None
-    if args.impl == "ours":
-        with torch.cuda.stream(stream):
-            step()  # eager warm-up on the capture stream
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            step()
-        run = graph.replay
-    else:
-        run = step
-        stream = torch.cuda.default_stream(dev)  # legacy default stream (the reference's)
 
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            run()
-    torch.cuda.synchronize()
-
-    # ---------------- timed region (device events, max over ranks)
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
-    barrier()
-    torch.cuda.synchronize()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
-        for _ in range(args.steps):
-            run()
-        ev1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    clk = clocks.stop()
-    ms_total = ev0.elapsed_time(ev1)
-    if world > 1 and args.impl == "ours":
-        t = torch.tensor([ms_total], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_total = float(t.item())
-    ms_step = ms_total / args.steps
-    tok_s = args.steps / (ms_total / 1e3)  # one token stream (tensor parallel at N > 1)
-
-    # ---------------- e2e: pinned H2D of the step input, replay, D2H token, per step
-    x_host = torch.empty_like(step.x, device="cpu").pin_memory()
-    x_host.copy_(step.x.cpu())
-    tok_host = torch.empty(1, dtype=torch.int32).pin_memory()
-    e2e_steps = max(5, args.steps // 2)
-    barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    with torch.cuda.stream(stream):
-        for _ in range(e2e_steps):
-            step.x.copy_(x_host, non_blocking=True)
-            run()
-            tok_host.copy_(step.tok, non_blocking=True)
-            stream.synchronize()
-            _ = int(tok_host[0])
-    e2e_s = time.perf_counter() - t0
-    if world > 1 and args.impl == "ours":
-        t = torch.tensor([e2e_s], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e = {"value": round(e2e_steps / e2e_s, 3), "unit": "tok/s",
-           "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
-           "d2h_bytes_per_step": tok_host.numel() * tok_host.element_size()}
-
-    result = {
-        "metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+def base_result(args, world, value, ms_step, clk, e2e, dtype):
+    return {
+        "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16" if args.impl == "ours" else "f16",
-        "data": "synthetic: random-init Llama-3.1-8B-shaped weights N(0,0.02) (seeded), N(0,1) hidden state",
+        "vs_baseline": None, "dtype": dtype,
+        "data": "synthetic: random-init Llama-3.1-8B weights N(0,0.02) (seeded), RMSNorm weights 1, "
+                f"{PROMPT}-token prompt uniform over the vocabulary (seeded)",
         "config": {
-            "workload": "bs=1 decode weight-matmul path of Llama-3.1-8B: 32 x [fused QKV+RoPE (KV cache row 2047), "
-                        "O, FFN gate/up+SwiGLU, FFN down] + lm_head+argmax",
-            "batch": 1, "hidden": H, "ffn": F, "vocab": V, "layers": L,
+            "workload": f"BASELINE config 5 at batch 1: greedy decode of random-init Llama-3.1-8B (32 layers, "
+                        f"hidden 4096, 32/8 heads, FFN 14336, vocab 128256) right after a {PROMPT}-token prompt",
+            "batch": 1, "prompt": PROMPT, "layers": L, "hidden": H, "ffn": F, "vocab": V,
             "weight_bytes_per_step": WEIGHT_BYTES,
             "l2": "inputs larger than L2 (15.01 GB of weights streamed per step)",
             "parallelism": f"tp{world}" if world > 1 else "single",
-            "tp_exchange": getattr(step, "mode", None),
-            "launch": "one CUDA graph per step" if args.impl == "ours" else "eager, legacy default stream",
         },
-        "matmul_hbm_gbs": round(WEIGHT_BYTES / (ms_step / 1e3) / 1e9, 1),
         "e2e": e2e,
         "clocks": clk,
     }
 
-    if args.impl == "ours":
-        result["gpu_launches"] = step.launches_per_step * args.steps
-        # dominant kernel (FFN gate/up + SwiGLU, 54% of the bytes): 32 launches over
-        # distinct layer weights per replay, timed with events on its stream
-        g2 = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g2, stream=stream):
-            step.gate_up_only()
-        reps = 10
-        with torch.cuda.stream(stream):
-            for _ in range(3):
-                g2.replay()
-            ev0.record(stream)
+
+def run_reference(torch, dev, args):
+    clocks = ClockSampler(0)
+    clocks.start()
+    time.sleep(0.3)
+    r = reference_decode(args.seed, args.steps, args.warmup)
+    clk = clocks.stop()
+    ms_step = r["decode_ms"] / args.steps
+    tok_s = args.steps / (r["decode_ms"] / 1e3)
+    e2e = {"value": round(tok_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4}
+    result = base_result(args, 1, tok_s, ms_step, clk, e2e, "f16")
+    result["impl"] = "reference"
+    result["config"]["launch"] = "the reference's decode_step loop: eager, legacy default stream, blocking D2H per token"
+    result["reference_build"] = ("Aryan470/infengine prefill.cu, decode.cu and kernels/*.cu compiled unchanged for "
+                                 "sm_100a (oracle/Makefile), cuBLAS 12.9; fp16 (its only dtype)")
+    result["prefill"] = {"prompt": PROMPT, "ms": round(r["prefill_ms"], 3),
+                         "tok_per_s": round(PROMPT / (r["prefill_ms"] / 1e3), 1)}
+    result["timing"] = "host wall clock around the reference's decode_step calls (each ends in a blocking copy)"
+    # the reference's weight-matmul path alone (its cuBLAS projections, RoPE,
+    # SwiGLU, lm_head and argmax kernels), eager on the legacy default stream
+    step = RefStep(torch, dev, args.seed)
+    ds = torch.cuda.default_stream(dev)
+    for _ in range(args.warmup):
+        step()
+    ms_mm = timed(torch, ds, lambda: [step() for _ in range(args.steps)], 1, dev) / args.steps
+    result["matmul_path"] = {"tok_per_s": round(1e3 / ms_mm, 3), "ms_per_step": round(ms_mm, 4),
+                             "hbm_gbs_per_gpu": round(WEIGHT_BYTES / (ms_mm / 1e3) / 1e9, 1)}
+    del step
+    if not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(args.seed)
+    print(json.dumps(result), flush=True)
+
+
+def run_ours(torch, dist, dev, args, world, rank, local, hbm_peak, tf_peak, tf_peak_sus, peak_src):
+    stream = torch.cuda.Stream(device=dev)
+    step = TPStep(torch, dev, args.seed, world, rank) if world > 1 else OursStep(torch, dev, args.seed)
+    torch.cuda.synchronize()
+    weights = full_model_weights(torch, dev, args.seed, step.layers, step.lm if world == 1 else step.inner.lm)
+    e2e_steps = max(5, args.steps // 2)
+    ctx = PROMPT + args.warmup + args.steps + e2e_steps + 64
+    eng = make_engine(weights, world, rank, 1, ctx, comm=getattr(step, "comm", None),
+                      exchange=getattr(step, "exchange", None), plan=getattr(step, "plan", None))
+    es = torch.cuda.ExternalStream(eng.stream, device=dev)
+    prompt = prompts(args.seed, 1)[0]
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    first = eng.prefill(0, prompt)
+    prefill_s = time.perf_counter() - t0
+    eng.decode(args.warmup)  # captures the step graph, then replays it
+
+    # ---------------- timed region: K decode steps (graph replays), device events
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    ms_total = timed(torch, es, lambda: eng.decode(args.steps), world, dev)
+    clk = clocks.stop()
+    ms_step = ms_total / args.steps
+    tok_s = args.steps / (ms_total / 1e3)
+
+    # ---------------- e2e: ie_engine_step, host token in and host id out per step
+    tok = np.array([first], np.int32)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        tok = eng.step(tok)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": round(e2e_steps / e2e_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+           "api": "ie_engine_step"}
+    result = base_result(args, world, tok_s, ms_step, clk, e2e, "bf16")
+    result["config"]["launch"] = "one CUDA graph per decode step (ie_engine_decode), ids kept on the device"
+    result["config"]["tp_exchange"] = getattr(step, "mode", None)
+    result["gpu_launches"] = (L * 7 + 4 + (1 if world > 1 else 0)) * args.steps
+    result["prefill_engine"] = {"prompt": PROMPT, "ms": round(prefill_s * 1e3, 3),
+                                "tok_per_s": round(PROMPT / prefill_s, 1), "timing": "host wall clock, blocking call"}
+    eng.close()
+    del eng, es
+    torch.cuda.synchronize()
+
+    # ---------------- the weight-matmul path alone (north-star target: >= 80 % of HBM)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        step()  # eager warm-up on the capture stream
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+
+    def replays():
+        for _ in range(args.steps):
+            graph.replay()
+    with torch.cuda.stream(stream):
+        ms_mm = timed(torch, stream, replays, world, dev) / args.steps
+    result["matmul_path"] = {
+        "workload": "32 x [fused QKV+RoPE (KV cache row 2047), O, FFN gate/up+SwiGLU, FFN down] + lm_head+argmax, "
+                    "bs=1 (no attention core, norms or residual adds)",
+        "tok_per_s": round(1e3 / ms_mm, 3), "ms_per_step": round(ms_mm, 4),
+        "hbm_gbs_per_gpu": round(WEIGHT_BYTES / world / (ms_mm / 1e3) / 1e9, 1),
+        "frac_of_hbm": round(WEIGHT_BYTES / world / (ms_mm / 1e3) / 1e9 / hbm_peak, 4),
+        "gpu_launches_per_step": step.launches_per_step,
+    }
+
+    # dominant kernel (FFN gate/up + SwiGLU, 54% of the bytes): 32 launches over
+    # distinct layer weights per replay, timed with events on its stream
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2, stream=stream):
+        step.gate_up_only()
+    reps = 10
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g2.replay()
+
+        def gu():
             for _ in range(reps):
                 g2.replay()
-            ev1.record(stream)
-        torch.cuda.synchronize()
-        per_launch_s = ev0.elapsed_time(ev1) / 1e3 / (reps * L)
-        f_local = step.h.shape[1]
-        gate_up_bytes = 2 * (2 * f_local * H + H + f_local)
-        achieved = gate_up_bytes / per_launch_s / 1e9
-        traffic = load_traffic()
-        result["roofline"] = {
-            "kernel": f"skinny_kernel<bf16,1,EPI_SWIGLU> (FFN gate/up + SwiGLU, M=1, {f_local} rows)",
-            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-            "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
-            "traffic": traffic if world == 1 else None, "algorithmic_bytes_per_launch": gate_up_bytes,
-            "avg_launch_us": round(per_launch_s * 1e6, 2),
-        }
-        result["step_roofline_frac"] = round(WEIGHT_BYTES / world / (ms_step / 1e3) / 1e9 / hbm_peak, 4)
-    if args.impl == "ours" and world > 1:
+        per_launch_s = timed(torch, stream, gu, world, dev) / 1e3 / (reps * L)
+    f_local = step.h.shape[1]
+    gate_up_bytes = 2 * (2 * f_local * H + H + f_local)
+    achieved = gate_up_bytes / per_launch_s / 1e9
+    traffic = load_traffic()
+    result["roofline"] = {
+        "kernel": f"skinny_kernel<bf16,1,EPI_SWIGLU> (FFN gate/up + SwiGLU, M=1, {f_local} rows)",
+        "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+        "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
+        "traffic": traffic if world == 1 else None, "algorithmic_bytes_per_launch": gate_up_bytes,
+        "avg_launch_us": round(per_launch_s * 1e6, 2),
+    }
+    del g2
+
+    if world > 1:
         # BASELINE config 3 under tensor parallelism: M=2048 projection chain,
         # per-rank shards on the tensor-core kernels, NCCL allreduce of the
         # fp32 O / down partials (32 MB each); aggregate TFLOP/s over ranks
@@ -680,14 +803,11 @@ def main():
             step.prefill()
         with torch.cuda.stream(stream):
             gp.replay()
-            ev0.record(stream)
-            for _ in range(3):
-                gp.replay()
-            ev1.record(stream)
-        torch.cuda.synchronize()
-        t = torch.tensor([ev0.elapsed_time(ev1) / 1e3 / 3], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        pre_s = float(t.item())
+
+            def pre():
+                for _ in range(3):
+                    gp.replay()
+            pre_s = timed(torch, stream, pre, world, dev) / 1e3 / 3
         tflops = step.prefill_flops() * world / pre_s / 1e12
         result["prefill"] = {"workload": f"M=2048 tokens, tp{world}: 32 x [QKV+RoPE, O+allreduce, gate/up+SwiGLU, "
                                          f"down+allreduce] + lm_head(last row)", "ms": round(pre_s * 1e3, 3),
@@ -695,7 +815,7 @@ def main():
                              "frac_of_n_x_sustained": round(tflops / (world * tf_peak_sus), 4)}
         gp.reset()
         del gp
-    if args.impl == "ours" and world == 1:
+    else:
         # prefill projection GEMMs at M=2048 over all 32 layers
         step.setup_prefill(2048)
         # BASELINE configs 1-4 one by one (before the long prefill chain, which
@@ -710,12 +830,11 @@ def main():
         reps = 3
         with torch.cuda.stream(stream):
             gp.replay()
-            ev0.record(stream)
-            for _ in range(reps):
-                gp.replay()
-            ev1.record(stream)
-        torch.cuda.synchronize()
-        pre_s = ev0.elapsed_time(ev1) / 1e3 / reps
+
+            def pre():
+                for _ in range(reps):
+                    gp.replay()
+            pre_s = timed(torch, stream, pre, world, dev) / 1e3 / reps
         tflops = step.prefill_flops() / pre_s / 1e12
         result["prefill"] = {
             "workload": "M=2048 tokens: 32 x [fused QKV+RoPE 6144x4096, O 4096x4096, gate/up+SwiGLU 2x14336x4096, "
@@ -725,43 +844,45 @@ def main():
             "gpu_launches": 4 * L,
         }
         del gp
-        # BASELINE config 5 shapes of the same path: batch-8 decode and the M=5
-        # verify pass (4 draft tokens + 1), same weights, one graph per step
-        for name, m in (("decode_bs8", 8), ("verify_m5", 5)):
-            sb = OursStep(torch, dev, args.seed, batch=m, layers=(step.layers, step.lm))
-            gb = torch.cuda.CUDAGraph()
-            with torch.cuda.stream(stream):
-                sb()
-            torch.cuda.synchronize()
-            with torch.cuda.graph(gb, stream=stream):
-                sb()
-            with torch.cuda.stream(stream):
-                for _ in range(3):
-                    gb.replay()
-                ev0.record(stream)
-                for _ in range(10):
-                    gb.replay()
-                ev1.record(stream)
-            torch.cuda.synchronize()
-            ms_b = ev0.elapsed_time(ev1) / 10
-            result[name] = {"rows": m, "ms_per_step": round(ms_b, 4), "tok_per_s": round(m / (ms_b / 1e3), 1),
-                            "hbm_gbs": round(WEIGHT_BYTES / (ms_b / 1e3) / 1e9, 1)}
-            del gb, sb
-        if rank == 0 and not args.no_cpu_baseline:
-            result["cpu_baseline"] = cpu_baseline(args.seed)
-    elif args.impl == "reference":
-        result["impl"] = "reference"
-        result["reference_build"] = ("Aryan470/infengine kernels/{ffn,swiglu,lm_head,sampling,attn,rope}.cu "
-                                     "compiled unchanged for sm_100a (oracle/Makefile), cuBLAS 12.9")
+        step.release_prefill()
+        torch.cuda.empty_cache()
+        # BASELINE config 5 at batch 8 and the M=5 verify pass, full model
+        B8, n8 = 8, 20
+        eng8 = make_engine(weights, 1, 0, B8, PROMPT + args.warmup + n8 + 16)
+        ps = prompts(args.seed, B8)
+        for b in range(B8):
+            eng8.prefill(b, ps[b])
+        eng8.decode(args.warmup)
+        es8 = torch.cuda.ExternalStream(eng8.stream, device=dev)
+        ms8 = timed(torch, es8, lambda: eng8.decode(n8), 1, dev) / n8
+        result["decode_bs8"] = {"batch": B8, "ms_per_step": round(ms8, 4), "tok_per_s": round(B8 / (ms8 / 1e3), 1),
+                                "steps": n8, "context": f"{PROMPT}-token prompts"}
+        eng8.close()
+        del eng8, es8
+        torch.cuda.synchronize()
+        eng5 = make_engine(weights, 1, 0, 1, PROMPT + 16)
+        nxt = eng5.prefill(0, prompt)
+        draft = np.concatenate([[nxt], prompts(args.seed + 1, 1)[0][:4]]).astype(np.int32)
+        for _ in range(3):
+            eng5.verify(0, draft)
+        es5 = torch.cuda.ExternalStream(eng5.stream, device=dev)
+        n5 = 20
+
+        def ver():
+            for _ in range(n5):
+                eng5.verify(0, draft)
+        ms5 = timed(torch, es5, ver, 1, dev) / n5
+        result["verify_m5"] = {"rows": 5, "ms_per_pass": round(ms5, 4), "tok_per_s": round(5 / (ms5 / 1e3), 1),
+                               "timing": "device events around blocking ie_engine_verify calls (host ids out)"}
+        eng5.close()
+        del eng5, es5
         if not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(args.seed)
 
     if rank == 0:
         print(json.dumps(result), flush=True)
     # graphs holding NCCL work are released before the communicators
-    run = None
-    if graph is not None:
-        graph.reset()
+    graph.reset()
     del graph
     torch.cuda.synchronize()
     if hasattr(step, "close"):

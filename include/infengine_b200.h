@@ -275,6 +275,9 @@ int ie_allreduce_sum_f32(ie_comm* comm, float* buf, size_t count, void* stream);
 int ie_argmax_allreduce(ie_comm* comm, unsigned long long* keys, int M, int* idx_out, void* stream);
 /* out[i] = round_dt(in[i]) for n values. */
 int ie_cast_f32(ie_dtype dt, const float* in, void* out, size_t n, void* stream);
+/* out[i] = round_dt(out[i] + round_dt(in[i])): a reduced row-split projection
+ * added to the residual stream (decode.cu:28,38). */
+int ie_add_f32(ie_dtype dt, const float* in, void* out, size_t n, void* stream);
 
 /* Row-split projection fused with its allreduce (decode, M <= 16): every
  * rank runs this on its column shard of X and W; each CTA pushes its fp32
@@ -350,6 +353,24 @@ typedef struct ie_engine ie_engine;
  * the longest chunk ie_engine_prefill accepts. */
 int ie_engine_create(ie_dtype dt, const ie_llama_desc* desc, int max_batch, int max_ctx, int max_prefill,
                      void* stream, ie_engine** out);
+/* Tensor-parallel engine, one per rank (Megatron split, as ShardPlan in the
+ * Python package describes): desc holds this rank's shards, so n_q_heads,
+ * n_kv_heads and ffn_dim are the local counts, wq/wk/wv/w_gate/w_up are the
+ * rank's rows, wo/w_down the rank's input columns; embedding and norms are
+ * full copies and vocab is the full vocabulary. lm_head holds lm_rows rows
+ * starting at global id lm_offset. O and down are reduced over the ranks
+ * (the NVLink exchange for decode rows when `exchange` is given, else NCCL)
+ * with the residual add fused; greedy ids are merged with a max over packed
+ * argmax keys (NCCL). Every rank must make the same calls in the same order. */
+typedef struct ie_engine_tp {
+  int world, rank;
+  ie_comm* comm;                    /* required */
+  const ie_tp_exchange* exchange;   /* nullable */
+  int lm_rows;
+  int64_t lm_offset;
+} ie_engine_tp;
+int ie_engine_create_tp(ie_dtype dt, const ie_llama_desc* desc, int max_batch, int max_ctx, int max_prefill,
+                        void* stream, const ie_engine_tp* tp, ie_engine** out);
 int ie_engine_destroy(ie_engine* eng);
 /* Append n tokens (host array) to sequence seq from its current position;
  * the greedy next token becomes the sequence's next input (and *next_token,
@@ -363,6 +384,12 @@ int ie_engine_decode(ie_engine* eng, int n_steps, int* out_tokens);
  * greedy id after row m. The cache rows are written; the position is not
  * moved (ie_engine_set_position accepts a prefix). */
 int ie_engine_verify(ie_engine* eng, int seq, const int* tokens, int M, int* out_ids);
+/* One greedy step of all max_batch sequences with host tokens: tokens_in
+ * [max_batch] (host) become the sequences' next inputs, tokens_out
+ * [max_batch] (host) receive the step's ids; the reference's decode_step
+ * contract (decode.cu:11-49: the token comes from and returns to the host).
+ * Blocks until done. */
+int ie_engine_step(ie_engine* eng, const int* tokens_in, int* tokens_out);
 int ie_engine_set_position(ie_engine* eng, int seq, int pos, int next_token);
 int ie_engine_position(const ie_engine* eng, int seq);
 void* ie_engine_stream(const ie_engine* eng);

@@ -58,7 +58,7 @@ EXPORTED_SYMBOLS = (
     "ie_ipc_export", "ie_ipc_import", "ie_ipc_release", "ie_gemm_allreduce", "ie_qkv_batched",
     "ie_attention_decode", "ie_gemm_add", "ie_gemm_allreduce_add", "ie_rmsnorm", "ie_embed", "ie_engine_create",
     "ie_engine_destroy", "ie_engine_prefill", "ie_engine_decode", "ie_engine_verify", "ie_engine_set_position",
-    "ie_engine_position", "ie_engine_stream",
+    "ie_engine_position", "ie_engine_stream", "ie_engine_step", "ie_engine_create_tp", "ie_add_f32",
 )
 
 

@@ -64,6 +64,14 @@ __global__ void cast_kernel(const float* in, T* out, size_t n) {
     out[i] = ie::DT<T>::from_f(in[i]);
 }
 
+// out[i] = round(out[i] + round(in[i])): the residual add of an allreduced
+// fp32 projection (the reference rounds the projection, then adds, decode.cu:28).
+template <typename T>
+__global__ void add_kernel(const float* in, T* out, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    out[i] = ie::DT<T>::from_f(ie::DT<T>::to_f(out[i]) + ie::round_to<T>(in[i]));
+}
+
 }  // namespace
 
 extern "C" {
@@ -129,6 +137,18 @@ int ie_cast_f32(ie_dtype dt, const float* in, void* out, size_t n, void* stream)
     cast_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(in, static_cast<__nv_bfloat16*>(out), n);
   else
     cast_kernel<__half><<<blocks, 256, 0, st>>>(in, static_cast<__half*>(out), n);
+  return cudaGetLastError() == cudaSuccess ? IE_OK : IE_ERR_LAUNCH;
+}
+
+int ie_add_f32(ie_dtype dt, const float* in, void* out, size_t n, void* stream) {
+  if ((dt != IE_DTYPE_F16 && dt != IE_DTYPE_BF16) || (n && (!in || !out))) return IE_ERR_INVALID_ARG;
+  if (n == 0) return IE_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int blocks = (int)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184);
+  if (dt == IE_DTYPE_BF16)
+    add_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(in, static_cast<__nv_bfloat16*>(out), n);
+  else
+    add_kernel<__half><<<blocks, 256, 0, st>>>(in, static_cast<__half*>(out), n);
   return cudaGetLastError() == cudaSuccess ? IE_OK : IE_ERR_LAUNCH;
 }
 

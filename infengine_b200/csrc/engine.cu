@@ -20,6 +20,11 @@
 //    decode.cu:47).
 //  * Verify runs M rows of one sequence (draft tokens) through the model at
 //    its current position and returns the greedy id after each row.
+//  * Tensor parallel (ie_engine_create_tp): every rank holds its shards; the
+//    O and down projections are reduced over the ranks with the residual add
+//    fused (NVLink exchange kernel for decode rows, NCCL otherwise) and the
+//    vocabulary-split lm_head is merged with a max over packed argmax keys.
+//    The collectives are captured in the same decode graph.
 //
 // Numerics are the library's kernels' (one rounding per projection as the
 // reference's cuBLAS calls, RMSNorm and residual add as the reference's
@@ -54,6 +59,15 @@ struct Engine {
   long long step_host = 0;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
+  // tensor parallelism (world == 1: single GPU)
+  int world = 1, rank = 0;
+  ie_comm* comm = nullptr;
+  bool has_ex = false;
+  ie_tp_exchange ex{};
+  int lm_rows = 0;
+  int64_t lm_offset = 0;
+  float* part = nullptr;               // fp32 [max_rows][H] partial sums (NCCL reduction)
+  unsigned long long* keys = nullptr;  // packed argmax keys [max(B, 16)]
 
   void* kcache(int l, int seq) const {
     return static_cast<char*>(kv) + ((size_t)l * layer_elems + (size_t)seq * cbs) * esz;
@@ -71,6 +85,20 @@ int check(cudaError_t e) { return e == cudaSuccess ? IE_OK : IE_ERR_LAUNCH; }
     const int s_ = (expr);       \
     if (s_ != IE_OK) return s_;  \
   } while (0)
+
+// x += round(X . W^T) for the O and down projections: one kernel on one GPU;
+// with tensor parallelism X and W are the rank's input columns and the
+// partial products are summed over the ranks before the rounding, by the
+// NVLink exchange kernel (decode rows) or NCCL (longer chunks).
+int proj_add(Engine& E, int M, int K, const void* X, const void* W) {
+  const int H = E.d.hidden;
+  if (E.world == 1) return ie_gemm_add(E.dt, M, H, K, X, K, W, K, E.x, H, E.st);
+  if (E.has_ex && M <= 16 && M <= E.ex.max_rows)
+    return ie_gemm_allreduce_add(E.dt, M, H, K, X, K, W, K, E.x, H, &E.ex, E.st);
+  IE_TRY(ie_gemm_f32out(E.dt, M, H, K, X, K, W, K, E.part, H, E.st));
+  IE_TRY(ie_allreduce_sum_f32(E.comm, E.part, (size_t)M * H, E.st));
+  return ie_add_f32(E.dt, E.part, E.x, (size_t)M * H, E.st);
+}
 
 // One transformer layer over M rows of the residual stream x. seq >= 0: the M
 // rows are consecutive tokens of sequence seq from position pos0 (prefill /
@@ -97,10 +125,10 @@ int layer_forward(Engine& E, int l, int M, int seq, int pos0) {
       IE_TRY(ie_attention(E.dt, M, pos0, nq, nkv, hd, E.q, (int64_t)M * hd, E.kcache(l, seq), E.vcache(l, seq), E.chs,
                           E.attn, (int64_t)nq * hd, st));
   }
-  IE_TRY(ie_gemm_add(E.dt, M, H, nq * hd, E.attn, (int64_t)nq * hd, w.wo, (int64_t)nq * hd, E.x, H, st));
+  IE_TRY(proj_add(E, M, nq * hd, E.attn, w.wo));
   IE_TRY(ie_rmsnorm(E.dt, M, H, E.x, H, w.ffn_norm, E.a, H, d.rms_eps, st));
   IE_TRY(ie_ffn_gate_up(E.dt, M, H, F, E.a, w.w_gate, w.w_up, E.h, F, st));
-  IE_TRY(ie_gemm_add(E.dt, M, H, F, E.h, F, w.w_down, F, E.x, H, st));
+  IE_TRY(proj_add(E, M, F, E.h, w.w_down));
   return IE_OK;
 }
 
@@ -109,8 +137,13 @@ int head_forward(Engine& E, int r0, int rows, int* ids_out) {
   const ie_llama_desc& d = E.d;
   const int H = d.hidden;
   IE_TRY(ie_rmsnorm(E.dt, rows, H, E.row(E.x, r0, H), H, d.final_norm, E.a, H, d.rms_eps, E.st));
-  return ie_lm_head_argmax(E.dt, rows, H, d.vocab, 0, E.a, H, d.lm_head, nullptr, 0, ids_out, nullptr, E.lm_ws,
-                           E.lm_ws_bytes, E.st);
+  if (E.world == 1)
+    return ie_lm_head_argmax(E.dt, rows, H, d.vocab, 0, E.a, H, d.lm_head, nullptr, 0, ids_out, nullptr, E.lm_ws,
+                             E.lm_ws_bytes, E.st);
+  // vocabulary shard: local winners as packed keys, then the max over ranks
+  IE_TRY(ie_lm_head_argmax(E.dt, rows, H, E.lm_rows, E.lm_offset, E.a, H, d.lm_head, nullptr, 0, nullptr, E.keys,
+                           E.lm_ws, E.lm_ws_bytes, E.st));
+  return ie_argmax_allreduce(E.comm, E.keys, rows, ids_out, E.st);
 }
 
 int decode_step(Engine& E) {
@@ -144,8 +177,8 @@ int capture(Engine& E) {
 void release(Engine* E) {
   if (E->exec) cudaGraphExecDestroy(E->exec);
   if (E->graph) cudaGraphDestroy(E->graph);
-  void* bufs[] = {E->x, E->a, E->q, E->attn, E->h, E->kv, E->tok_in, E->positions, E->history, E->step, E->chunk,
-                  E->ids, E->lm_ws};
+  void* bufs[] = {E->x,       E->a,     E->q,    E->attn,  E->h,     E->kv,    E->tok_in, E->positions,
+                  E->history, E->step,  E->chunk, E->ids,  E->lm_ws, E->part, E->keys};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (E->own_stream && E->st) cudaStreamDestroy(E->st);
@@ -175,12 +208,32 @@ extern "C" {
 
 int ie_engine_create(ie_dtype dt, const ie_llama_desc* desc, int max_batch, int max_ctx, int max_prefill,
                      void* stream, ie_engine** out) {
+  return ie_engine_create_tp(dt, desc, max_batch, max_ctx, max_prefill, stream, nullptr, out);
+}
+
+int ie_engine_create_tp(ie_dtype dt, const ie_llama_desc* desc, int max_batch, int max_ctx, int max_prefill,
+                        void* stream, const ie_engine_tp* tp, ie_engine** out) {
   if (!out) return IE_ERR_INVALID_ARG;
   *out = nullptr;
   if ((dt != IE_DTYPE_F16 && dt != IE_DTYPE_BF16) || !valid_desc(desc)) return IE_ERR_INVALID_ARG;
   if (max_batch <= 0 || max_batch > 64 || max_ctx <= 0 || max_prefill < 0) return IE_ERR_INVALID_ARG;
+  if (tp && tp->world > 1) {
+    if (tp->rank < 0 || tp->rank >= tp->world || !tp->comm || tp->lm_rows <= 0 || tp->lm_offset < 0 ||
+        tp->lm_offset + tp->lm_rows > desc->vocab)
+      return IE_ERR_INVALID_ARG;
+    if (tp->exchange && (tp->exchange->world != tp->world || tp->exchange->rank != tp->rank)) return IE_ERR_INVALID_ARG;
+  }
   Engine* E = new (std::nothrow) Engine();
   if (!E) return IE_ERR_INVALID_ARG;
+  if (tp && tp->world > 1) {
+    E->world = tp->world;
+    E->rank = tp->rank;
+    E->comm = tp->comm;
+    E->has_ex = tp->exchange != nullptr;
+    if (tp->exchange) E->ex = *tp->exchange;
+    E->lm_rows = tp->lm_rows;
+    E->lm_offset = tp->lm_offset;
+  }
   E->dt = dt;
   E->d = *desc;
   E->layers.assign(desc->layers, desc->layers + desc->n_layers);
@@ -219,6 +272,10 @@ int ie_engine_create(ie_dtype dt, const ie_llama_desc* desc, int max_batch, int 
   alloc(reinterpret_cast<void**>(&E->chunk), R * sizeof(int));
   alloc(reinterpret_cast<void**>(&E->ids), R * sizeof(int));
   alloc(&E->lm_ws, E->lm_ws_bytes);
+  if (E->world > 1) {
+    alloc(reinterpret_cast<void**>(&E->part), R * H * sizeof(float));
+    alloc(reinterpret_cast<void**>(&E->keys), (size_t)(max_batch > 16 ? max_batch : 16) * sizeof(unsigned long long));
+  }
   if (ok) {
     ok = cudaMemsetAsync(E->kv, 0, (size_t)d.n_layers * E->layer_elems * 2, E->st) == cudaSuccess &&
          cudaMemsetAsync(E->tok_in, 0, max_batch * sizeof(int), E->st) == cudaSuccess &&
@@ -307,6 +364,23 @@ int ie_engine_verify(ie_engine* eng, int seq, const int* tokens, int M, int* out
   IE_TRY(head_forward(E, 0, M, E.ids));
   IE_TRY(check(cudaMemcpyAsync(out_ids, E.ids, M * sizeof(int), cudaMemcpyDeviceToHost, E.st)));
   return check(cudaStreamSynchronize(E.st));
+}
+
+int ie_engine_step(ie_engine* eng, const int* tokens_in, int* tokens_out) {
+  if (!eng || !tokens_in || !tokens_out) return IE_ERR_INVALID_ARG;
+  Engine& E = *eng->e;
+  for (int b = 0; b < E.B; ++b) {
+    if (tokens_in[b] < 0 || tokens_in[b] >= E.d.vocab) return IE_ERR_INVALID_ARG;
+    if (E.pos_host[b] + 1 > E.ctx) return IE_ERR_UNSUPPORTED;
+  }
+  IE_TRY(capture(E));
+  IE_TRY(check(cudaMemcpyAsync(E.tok_in, tokens_in, E.B * sizeof(int), cudaMemcpyHostToDevice, E.st)));
+  IE_TRY(check(cudaGraphLaunch(E.exec, E.st)));
+  IE_TRY(check(cudaMemcpyAsync(tokens_out, E.tok_in, E.B * sizeof(int), cudaMemcpyDeviceToHost, E.st)));
+  IE_TRY(check(cudaStreamSynchronize(E.st)));
+  E.step_host += 1;
+  for (int b = 0; b < E.B; ++b) E.pos_host[b] += 1;
+  return IE_OK;
 }
 
 int ie_engine_set_position(ie_engine* eng, int seq, int pos, int next_token) {

@@ -30,6 +30,11 @@ class LlamaDesc(ctypes.Structure):
                 ("rope_cos", _vp), ("rope_sin", _vp)]
 
 
+class EngineTP(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int), ("comm", _vp), ("exchange", _vp),
+                ("lm_rows", ctypes.c_int), ("lm_offset", ctypes.c_int64)]
+
+
 _bound = False
 
 
@@ -40,6 +45,9 @@ def _bind():
     L = lib()
     i32, vp = ctypes.c_int, ctypes.c_void_p
     L.ie_engine_create.argtypes = [i32, ctypes.POINTER(LlamaDesc), i32, i32, i32, vp, ctypes.POINTER(vp)]
+    L.ie_engine_create_tp.argtypes = [i32, ctypes.POINTER(LlamaDesc), i32, i32, i32, vp, ctypes.POINTER(EngineTP),
+                                      ctypes.POINTER(vp)]
+    L.ie_engine_step.argtypes = [vp, vp, vp]
     L.ie_engine_destroy.argtypes = [vp]
     L.ie_engine_prefill.argtypes = [vp, i32, vp, i32, vp]
     L.ie_engine_decode.argtypes = [vp, i32, vp]
@@ -68,7 +76,11 @@ class LlamaEngine:
     """
 
     def __init__(self, weights: dict, dims: dict, dtype: str = "bf16", max_batch: int = 1, max_ctx: int = 4096,
-                 max_prefill: int = 2048):
+                 max_prefill: int = 2048, tp: dict | None = None):
+        """tp (tensor parallel, one engine per rank): dict with world, rank,
+        comm (infengine_b200.tp.Comm), exchange (tp.P2PExchange or None),
+        lm_rows and lm_offset; weights then hold this rank's shards and dims
+        the local head / FFN counts (vocab stays the full vocabulary)."""
         _bind()
         self.B = max_batch
         self._layers = (LayerWeights * dims["n_layers"])()
@@ -81,8 +93,16 @@ class LlamaEngine:
         self._keep = weights  # the engine reads these buffers
         h = ctypes.c_void_p()
         dt = IE_DTYPE_BF16 if dtype == "bf16" else IE_DTYPE_F16
-        _check(lib().ie_engine_create(dt, ctypes.byref(self.desc), max_batch, max_ctx, max_prefill, None,
-                                      ctypes.byref(h)), "ie_engine_create")
+        if tp is None:
+            _check(lib().ie_engine_create(dt, ctypes.byref(self.desc), max_batch, max_ctx, max_prefill, None,
+                                          ctypes.byref(h)), "ie_engine_create")
+        else:
+            ex = tp.get("exchange")
+            self._tp = EngineTP(tp["world"], tp["rank"], tp["comm"].handle,
+                                ctypes.addressof(ex.desc) if ex is not None else None, tp["lm_rows"], tp["lm_offset"])
+            self._tp_keep = (tp["comm"], ex)
+            _check(lib().ie_engine_create_tp(dt, ctypes.byref(self.desc), max_batch, max_ctx, max_prefill, None,
+                                             ctypes.byref(self._tp), ctypes.byref(h)), "ie_engine_create_tp")
         self.h = h
 
     def prefill(self, seq: int, tokens) -> int:
@@ -96,6 +116,13 @@ class LlamaEngine:
         """[n_steps, max_batch] greedy ids (row i: the ids produced by step i)."""
         out = np.zeros((n_steps, self.B), np.int32)
         _check(lib().ie_engine_decode(self.h, n_steps, out.ctypes.data_as(_vp)), "ie_engine_decode")
+        return out
+
+    def step(self, tokens_in) -> np.ndarray:
+        """One greedy step with host tokens in and out (ie_engine_step)."""
+        t = np.ascontiguousarray(tokens_in, dtype=np.int32)
+        out = np.zeros(self.B, np.int32)
+        _check(lib().ie_engine_step(self.h, t.ctypes.data_as(_vp), out.ctypes.data_as(_vp)), "ie_engine_step")
         return out
 
     def verify(self, seq: int, tokens) -> np.ndarray:

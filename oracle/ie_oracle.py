@@ -359,3 +359,61 @@ def attention(q, k, v, pos0: int, dt: str):
             out[s, h * D:(h + 1) * D] = round_dt((p.astype(np.float64) @ v[hk, :L].astype(np.float64)).astype(np.float32),
                                                  dt)
     return out
+
+
+# ------------------------------------------- the decode step around the path
+def rmsnorm(x, w, dt: str, eps: float = 1e-5):
+    """kernels/rmsnorm.cu:29-62: scale = rsqrt(sum(x^2) / H + eps) per row,
+    out = round(round(x * scale) * w). The sum is taken exactly and rounded
+    once to fp32 (the reference's fp32 tree can differ in the last bit)."""
+    x = np.asarray(x, dtype=np.float32)
+    ss = (x.astype(np.float64) ** 2).sum(axis=-1, keepdims=True).astype(np.float32)
+    scale = (np.float32(1.0) / np.sqrt(ss / np.float32(x.shape[-1]) + np.float32(eps))).astype(np.float32)
+    return round_dt(round_dt(x * scale, dt) * np.asarray(w, dtype=np.float32), dt)
+
+
+def residual_add(x, delta, dt: str):
+    """kernels/residual_add.cu:10-20: x = round(x + delta)."""
+    return round_dt(np.asarray(x, dtype=np.float32) + np.asarray(delta, dtype=np.float32), dt)
+
+
+class LlamaOracle:
+    """The reference's request flow on the CPU (prefill.cu:11-48 then
+    decode.cu:11-49 per token, manager.cpp:31-86), built from the functions
+    above, for small models: weights is a dict of float32 arrays holding
+    dt-representable values (embedding [V,H], final_norm [H], lm_head [V,H],
+    layers: list of dicts attn_norm, wq, wk, wv, wo, ffn_norm, w_gate, w_up,
+    w_down). Keeps the K/V cache between calls."""
+
+    def __init__(self, weights: dict, n_q_heads: int, n_kv_heads: int, dt: str, max_ctx: int = 4096,
+                 eps: float = 1e-5):
+        self.w, self.nq, self.nkv, self.dt, self.eps = weights, n_q_heads, n_kv_heads, dt, eps
+        self.cos, self.sin = rope_tables(max_ctx)
+        L = len(weights["layers"])
+        self.k = np.zeros((L, n_kv_heads, max_ctx, HEAD_DIM), np.float32)
+        self.v = np.zeros_like(self.k)
+        self.pos = 0
+
+    def forward(self, tokens):
+        """Run the rows of `tokens` from the current position; returns the
+        rounded logits of every row and advances the position."""
+        dt, w = self.dt, self.w
+        x = w["embedding"][np.asarray(tokens)]
+        S, pos0 = len(tokens), self.pos
+        for l, lw in enumerate(w["layers"]):
+            a = rmsnorm(x, lw["attn_norm"], dt, self.eps)
+            q, k, v = qkv(a, lw["wq"], lw["wk"], lw["wv"], dt, pos0, self.cos, self.sin)
+            self.k[l, :, pos0:pos0 + S] = k
+            self.v[l, :, pos0:pos0 + S] = v
+            att = attention(q, self.k[l], self.v[l], pos0, dt)
+            x = residual_add(x, multiply_by_weight(att, lw["wo"], dt), dt)
+            a = rmsnorm(x, lw["ffn_norm"], dt, self.eps)
+            x = residual_add(x, ffn(a, lw["w_gate"], lw["w_up"], lw["w_down"], dt), dt)
+        self.pos += S
+        return multiply_by_weight(rmsnorm(x, w["final_norm"], dt, self.eps), w["lm_head"], dt)
+
+    @staticmethod
+    def pick(logits_row):
+        """Greedy id (the reference's tie order) and the top-1 minus top-2 margin."""
+        top2 = np.sort(logits_row)[-2:]
+        return argmax_reference_fast(logits_row), float(top2[1] - top2[0])

@@ -203,3 +203,20 @@ def test_engine_rejects_bad_input(ie, cuda):
     with pytest.raises(IEError):
         e.decode(64)                             # past max_ctx
     e.close()
+
+
+@pytest.mark.parametrize("prompt_len", [12, 40])
+def test_engine_matches_model_oracle(ie, cuda, prompt_len):
+    """The whole model against the CPU oracle on a tiny random-init Llama:
+    prompts of 12 tokens (decode kernels, exact attention chain) and 40
+    tokens (tensor-core GEMMs, flash attention), then teacher-forced steps
+    through ie_engine_step. An id may differ only where the oracle's top-2
+    margin is within rounding noise."""
+    from tiny_model import engine_vs_oracle, tiny_weights
+    weights = tiny_weights(oracle, layers=2, seed=prompt_len)
+    prompt = np.random.default_rng(1).integers(0, 1000, size=prompt_len).astype(np.int32)
+    got, want, margin = engine_vs_oracle(oracle, to_dev, weights, prompt, 12)
+    bad = got != want
+    print(f"engine vs model oracle: {(~bad).sum()}/{len(got)} ids equal; margins at differences {margin[bad]}")
+    assert (~bad).mean() >= 0.8
+    assert np.all(margin[bad] < 0.03), (got, want, margin)
