@@ -618,6 +618,9 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    # NCCL writes its log (the version banner included, when NCCL_DEBUG is
+    # set) to stdout by default; stdout carries only the JSON line here
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     if args.impl == "reference":
         if rank != 0:  # the reference runs on one GPU; other ranks have no work
             return
@@ -698,6 +701,9 @@ def run_ours(torch, dist, dev, args, world, rank, local, hbm_peak, tf_peak, tf_p
                       exchange=getattr(step, "exchange", None), plan=getattr(step, "plan", None))
     es = torch.cuda.ExternalStream(eng.stream, device=dev)
     prompt = prompts(args.seed, 1)[0]
+    # untimed warm-up prefill (first-call setup: tensor maps, NCCL connections)
+    eng.prefill(0, prompt[:256])
+    eng.set_position(0, 0, 0)
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
