@@ -111,12 +111,17 @@ __device__ __forceinline__ bool fd_wait(uint32_t bar, uint32_t parity, volatile 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ float ld_cluster(const float* local, unsigned rank) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(fd_smem_u32(local)), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-  return v;
+// The same shared-memory word of every CTA of the cluster (rank order). The
+// loads carry no memory clobber: they follow a cluster barrier and are all
+// issued before any is used.
+__device__ __forceinline__ void ld_cluster_all(const float* local, float (&v)[kFdCluster]) {
+  const uint32_t a = fd_smem_u32(local);
+#pragma unroll
+  for (unsigned r = 0; r < kFdCluster; ++r) {
+    uint32_t remote;
+    asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(a), "r"(r));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v[r]) : "r"(remote));
+  }
 }
 
 // Warp sum of G per-lane values, transposed on the way: at the level with
@@ -312,7 +317,9 @@ __global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
   cluster_sync_all();
   if (tid < G) {
     float v = -INFINITY;
-    for (unsigned r = 0; r < kFdCluster; ++r) v = fmaxf(v, ld_cluster(&cmax[tid], r));
+    float all[kFdCluster];
+    ld_cluster_all(&cmax[tid], all);
+    for (unsigned r = 0; r < kFdCluster; ++r) v = fmaxf(v, all[r]);
     gmax[tid] = v;
   }
   __syncthreads();
@@ -344,7 +351,9 @@ __global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
   cluster_sync_all();
   if (tid < G) {
     float v = 0.f;
-    for (unsigned r = 0; r < kFdCluster; ++r) v += ld_cluster(&csum[tid], r);
+    float all[kFdCluster];
+    ld_cluster_all(&csum[tid], all);
+    for (unsigned r = 0; r < kFdCluster; ++r) v += all[r];
     ginv[tid] = 1.0f / v;
   }
   __syncthreads();
@@ -404,7 +413,9 @@ __global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
   if (tid < kPer) {
     const int e = (int)rank * kPer + tid;
     float s = 0.f;
-    for (unsigned r = 0; r < kFdCluster; ++r) s += ld_cluster(&opart[e], r);
+    float all[kFdCluster];
+    ld_cluster_all(&opart[e], all);
+    for (unsigned r = 0; r < kFdCluster; ++r) s += all[r];
     const int h = e >> 7, d = e & 127;
     static_cast<T*>(p.out)[(int64_t)m * p.ld_out + (int64_t)(hk * G + h) * 128 + d] = DT<T>::from_f(s);
   }

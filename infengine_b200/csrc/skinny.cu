@@ -71,6 +71,9 @@ constexpr int kThreads = kWarps * 32;
 #ifndef IE_SK_MINBLOCKS
 #define IE_SK_MINBLOCKS 1  // __launch_bounds__ minimum resident CTAs per SM (register cap)
 #endif
+#ifndef IE_SK_MINBLOCKS_MT1
+#define IE_SK_MINBLOCKS_MT1 IE_SK_MINBLOCKS  // the same for M <= 8 (one n-tile of activation rows)
+#endif
 #ifndef IE_SK_EARLY_W
 #define IE_SK_EARLY_W 0  // 1: first weight batch requested before waiting for the previous kernel
 #endif
@@ -365,7 +368,8 @@ struct Batch {
 // loads of its next batch before the MMAs of the current one, so it always
 // has loads in flight.
 template <typename T, int MT, int EPI>
-__global__ void __launch_bounds__(kThreads, IE_SK_MINBLOCKS) skinny_kernel(const SkinnyParams p) {
+__global__ void __launch_bounds__(kThreads, MT == 1 ? IE_SK_MINBLOCKS_MT1 : IE_SK_MINBLOCKS)
+    skinny_kernel(const SkinnyParams p) {
   constexpr int NMAT = EpiTraits<EPI>::nmat;
   constexpr int NR = NMAT * MT * 4;
   __shared__ float red[kWarps][NR][32];
