@@ -56,6 +56,7 @@ H, F, V, L = 4096, 14336, 128256, 32
 NQ, NKV, HD, CTX = 32, 8, 128, 8192
 POS = 2047  # the 2048th token: decode right after a 2048-token prompt
 PROMPT = 2048
+JSON_OUT = None  # the original stdout (see main)
 LAYER_WEIGHT_ELEMS = (NQ + 2 * NKV) * HD * H + H * H + 3 * F * H
 WEIGHT_BYTES = 2 * (L * LAYER_WEIGHT_ELEMS + V * H)
 GATE_UP_BYTES = 2 * (2 * F * H + H + F)  # one gate/up+SwiGLU launch at M=1
@@ -618,9 +619,12 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    # NCCL writes its log (the version banner included, when NCCL_DEBUG is
-    # set) to stdout by default; stdout carries only the JSON line here
-    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+    # stdout carries only the JSON line: whatever the libraries print on file
+    # descriptor 1 (NCCL's version banner, for one) goes to stderr instead
+    global JSON_OUT
+    sys.stdout.flush()
+    JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     if args.impl == "reference":
         if rank != 0:  # the reference runs on one GPU; other ranks have no work
             return
@@ -687,7 +691,13 @@ def run_reference(torch, dev, args):
     del step
     if not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args.seed)
-    print(json.dumps(result), flush=True)
+    emit(result)
+
+
+def emit(result):
+    out = JSON_OUT if JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(result) + "\n")
+    out.flush()
 
 
 def run_ours(torch, dist, dev, args, world, rank, local, hbm_peak, tf_peak, tf_peak_sus, peak_src):
@@ -886,7 +896,7 @@ def run_ours(torch, dist, dev, args, world, rank, local, hbm_peak, tf_peak, tf_p
             result["cpu_baseline"] = cpu_baseline(args.seed)
 
     if rank == 0:
-        print(json.dumps(result), flush=True)
+        emit(result)
     # graphs holding NCCL work are released before the communicators
     graph.reset()
     del graph

@@ -394,6 +394,35 @@ int ie_engine_set_position(ie_engine* eng, int seq, int pos, int next_token);
 int ie_engine_position(const ie_engine* eng, int seq);
 void* ie_engine_stream(const ie_engine* eng);
 
+/* ---- safetensors weight loading ---------------------------------------------
+ * Replaces ModelWeights::from_safetensors (kernels/model_weights.cu:80-154)
+ * without a JSON library. ie_st_* read a file's header (host only, no GPU
+ * needed); ie_llama_load puts one rank's weights of a Hugging Face Llama
+ * checkpoint (model.embed_tokens / model.layers.N.{input_layernorm,
+ * self_attn.{q,k,v,o}_proj, post_attention_layernorm, mlp.{gate,up,down}_proj}
+ * / model.norm / lm_head, tied embeddings accepted) into one device slab in
+ * dt, sharded for rank `rank` of `world` as ie_engine_create_tp expects, plus
+ * the RoPE tables for max_ctx positions. The desc it returns is ready for
+ * ie_engine_create / ie_engine_create_tp (with ie_llama_model_shard giving
+ * lm_rows and lm_offset) and lives as long as the model. */
+#define IE_ST_OTHER 0
+#define IE_ST_BF16  1
+#define IE_ST_F16   2
+#define IE_ST_F32   3
+typedef struct ie_safetensors ie_safetensors;
+int ie_st_open(const char* path, ie_safetensors** out);
+int ie_st_close(ie_safetensors* f);
+int ie_st_count(const ie_safetensors* f);
+const char* ie_st_name(const ie_safetensors* f, int i);
+/* shape: room for 8 dimensions */
+int ie_st_info(const ie_safetensors* f, const char* name, int* dtype, int* ndim, int64_t* shape, uint64_t* nbytes);
+typedef struct ie_llama_model ie_llama_model;
+int ie_llama_load(const char* const* paths, int n_paths, ie_dtype dt, int world, int rank, int max_ctx,
+                  float rms_eps, void* stream, ie_llama_model** out);
+const ie_llama_desc* ie_llama_model_desc(const ie_llama_model* m);
+int ie_llama_model_shard(const ie_llama_model* m, int* lm_rows, int64_t* lm_offset);
+int ie_llama_model_free(ie_llama_model* m);
+
 /* Global vocabulary id held in a packed argmax key. */
 static inline int ie_argmax_key_index(unsigned long long key) {
   unsigned int tie = ~(unsigned int)(key & 0xffffffffull);

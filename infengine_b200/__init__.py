@@ -59,6 +59,8 @@ EXPORTED_SYMBOLS = (
     "ie_attention_decode", "ie_gemm_add", "ie_gemm_allreduce_add", "ie_rmsnorm", "ie_embed", "ie_engine_create",
     "ie_engine_destroy", "ie_engine_prefill", "ie_engine_decode", "ie_engine_verify", "ie_engine_set_position",
     "ie_engine_position", "ie_engine_stream", "ie_engine_step", "ie_engine_create_tp", "ie_add_f32",
+    "ie_st_open", "ie_st_close", "ie_st_count", "ie_st_name", "ie_st_info", "ie_llama_load", "ie_llama_model_desc",
+    "ie_llama_model_shard", "ie_llama_model_free",
 )
 
 

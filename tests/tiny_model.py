@@ -24,19 +24,22 @@ def tiny_weights(oracle, layers: int, seed: int, dt: str = "bf16"):
                              w_gate=w(F, H), w_up=w(F, H), w_down=w(H, F)) for _ in range(layers)])
 
 
-def engine_vs_oracle(oracle, to_dev, weights: dict, prompt, n_steps: int, dt: str = "bf16", max_ctx: int = 256):
+def engine_vs_oracle(oracle, to_dev, weights: dict, prompt, n_steps: int, dt: str = "bf16", max_ctx: int = 256,
+                     eng=None):
     """Prefill `prompt`, then n_steps teacher-forced steps (both sides fed the
-    oracle's ids). Returns (engine ids, oracle ids, oracle margins)."""
+    oracle's ids); `eng`: an engine on these weights (default: one built
+    here from device copies). Returns (engine ids, oracle ids, oracle margins)."""
     import torch
     from infengine_b200.engine import LlamaEngine
     layers = weights["layers"]
-    dev_w = {k: to_dev(v, dt) for k, v in weights.items() if k != "layers"}
-    dev_w["layers"] = [{k: to_dev(v, dt) for k, v in lw.items()} for lw in layers]
-    cos, sin = oracle.rope_tables(max_ctx)
-    dev_w["rope_cos"] = torch.from_numpy(cos).cuda()
-    dev_w["rope_sin"] = torch.from_numpy(sin).cuda()
-    dims = dict(TINY, n_layers=len(layers))
-    eng = LlamaEngine(dev_w, dims, dtype=dt, max_batch=1, max_ctx=max_ctx, max_prefill=max(len(prompt), 16))
+    if eng is None:
+        dev_w = {k: to_dev(v, dt) for k, v in weights.items() if k != "layers"}
+        dev_w["layers"] = [{k: to_dev(v, dt) for k, v in lw.items()} for lw in layers]
+        cos, sin = oracle.rope_tables(max_ctx)
+        dev_w["rope_cos"] = torch.from_numpy(cos).cuda()
+        dev_w["rope_sin"] = torch.from_numpy(sin).cuda()
+        dims = dict(TINY, n_layers=len(layers))
+        eng = LlamaEngine(dev_w, dims, dtype=dt, max_batch=1, max_ctx=max_ctx, max_prefill=max(len(prompt), 16))
     ref = oracle.LlamaOracle(weights, TINY["n_q_heads"], TINY["n_kv_heads"], dt, max_ctx=max_ctx)
     got = [eng.prefill(0, prompt)]
     want, margin = [], []
