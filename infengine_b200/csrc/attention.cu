@@ -38,6 +38,9 @@
 //    the launch's first query row are requested before the kernel waits for
 //    its predecessor (programmatic launch), so their latency overlaps the
 //    QKV projection's tail.
+//  * Scores run on the tensor cores (m16n8k16: 16 cache rows x the group's
+//    query heads, padded to 8, per instruction), the A operand read straight
+//    from the copied rows, q held in B fragments.
 //  * The softmax keeps the reference's chain (scores rounded, scaled and
 //    rounded; e = exp(t - max) summed in fp32 and stored rounded;
 //    p = round(round(e) * (1/sum))): the row maximum and the sum are exact
@@ -124,28 +127,25 @@ __device__ __forceinline__ void ld_cluster_all(const float* local, float (&v)[kF
   }
 }
 
-// Warp sum of G per-lane values, transposed on the way: at the level with
-// offset 16 >> l the lanes with that bit set keep the upper half of their
-// values. Lane l ends with the full sum of value l / (32 / G).
-template <int G>
-__device__ __forceinline__ float warp_sum_transposed(float (&s)[G], int lane) {
-  float v[G];
-#pragma unroll
-  for (int i = 0; i < G; ++i) v[i] = s[i];
-#pragma unroll
-  for (int lvl = 0; (1 << lvl) < G; ++lvl) {
-    const int off = 16 >> lvl, w = G >> lvl;
-    const bool upper = (lane & off) != 0;
-#pragma unroll
-    for (int i = 0; i < w / 2; ++i) {
-      const float keep = upper ? v[i + w / 2] : v[i];
-      const float send = upper ? v[i] : v[i + w / 2];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-    }
-  }
-#pragma unroll
-  for (int off = 16 / G; off > 0; off >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
-  return v[0];
+// m16n8k16 tensor-core product, fp32 accumulation (A and B of the same type).
+template <typename T>
+__device__ __forceinline__ void fd_mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                       uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __half>::value)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t fd_pack2(float lo, float hi) {
+  T a = DT<T>::from_f(lo), b = DT<T>::from_f(hi);
+  return (uint32_t)(*reinterpret_cast<uint16_t*>(&a)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&b)) << 16);
 }
 
 template <typename T, int G>
@@ -155,6 +155,7 @@ __global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
   __shared__ float qf[G][128];
   __shared__ float opart[G * 128];
   __shared__ float red[kFdWarps][G];
+  __shared__ float spart[2][kFdRows][G];  // half-dimension partial scores of a chunk
   __shared__ float cmax[G], csum[G], gmax[G], ginv[G];
   __shared__ __align__(8) unsigned long long bars[kFdStages];
   __shared__ int abort_s, fail_at;
@@ -240,11 +241,20 @@ __global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
     qf[h][d] = DT<T>::to_f(static_cast<const T*>(p.q)[(int64_t)(hk * G + h) * p.q_head_stride + (int64_t)m * 128 + d]);
   }
   __syncthreads();
-  float qr[G][4];
+  // B fragments of q for the score MMAs. Warp w multiplies the 16-row tile
+  // w & 3 of a chunk over head dimensions [64 (w >> 2), +64); lane (g, t)
+  // holds, for each 32-dimension k-step, the 8 dimensions 8t .. 8t+7 of head g
+  // (zero for g >= G) in the order its A chunks use (the same k permutation as
+  // the decode GEMV: MMA j takes elements 4j .. 4j+3 of the chunk).
+  const int fg = lane >> 2, ft = lane & 3, tile_w = warp & 3, half_w = warp >> 2;
+  uint32_t qb[2][4];
 #pragma unroll
-  for (int h = 0; h < G; ++h)
+  for (int ks = 0; ks < 2; ++ks)
 #pragma unroll
-    for (int d = 0; d < 4; ++d) qr[h][d] = qf[h][lane * 4 + d];
+    for (int e2 = 0; e2 < 4; ++e2) {
+      const int d = 64 * half_w + 32 * ks + 8 * ft + 2 * e2;
+      qb[ks][e2] = fg < G ? fd_pack2<T>(qf[fg][d], qf[fg][d + 1]) : 0u;
+    }
 
   auto wait_chunk = [&](int i) {
     if (!fd_wait(fd_smem_u32(&bars[i % kFdStages]), (uint32_t)((i / kFdStages) & 1), &abort_s))
@@ -255,42 +265,38 @@ __global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
     if (tid == 0 && !abort_s && i + kFdStages < total) issue(i + kFdStages);
   };
 
-  // ---- scores: warp per cache row, lane per 4 dims
+  // ---- scores on the tensor cores: S[row][head] = K[row] . q[head], one
+  // m16n8k16 per 16 dimensions; the two dimension halves of a tile meet in
+  // shared memory (low half + high half), then round, scale, round
   const float scale = rsqrtf(128.0f);
   for (int i = 0; i < nk; ++i) {
     wait_chunk(i);
     const T* tile = ring + (i % kFdStages) * kFdRows * 128;
     const int r0 = i * kFdRows, rows = min(kFdRows, n - r0);
-    // four rows per warp at a time: independent loads and shuffle chains
-    for (int rb = warp; rb < rows; rb += 4 * kFdWarps) {
-      uint2 raw[4];
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    const T* ra = tile + (tile_w * 16 + fg) * 128 + 64 * half_w + 8 * ft;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int r = rb + u * kFdWarps;
-        raw[u] = r < rows ? *reinterpret_cast<const uint2*>(tile + r * 128 + lane * 4) : make_uint2(0, 0);
-      }
-      float v[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const T* e = reinterpret_cast<const T*>(&raw[u]);
-        float s[G];
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-          float a = qr[h][0] * DT<T>::to_f(e[0]);
-#pragma unroll
-          for (int d = 1; d < 4; ++d) a = fmaf(qr[h][d], DT<T>::to_f(e[d]), a);
-          s[h] = a;
-        }
-        v[u] = warp_sum_transposed<G>(s, lane);
-      }
-      if ((lane & (32 / G - 1)) == 0) {
-        const int h = lane / (32 / G);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int r = rb + u * kFdWarps;
-          if (r < rows) sc[h * p.cap + r0 + r] = DT<T>::from_f(round_to<T>(round_to<T>(v[u]) * scale));
-        }
-      }
+    for (int ks = 0; ks < 2; ++ks) {
+      const uint4 wa = *reinterpret_cast<const uint4*>(ra + 32 * ks);            // row g
+      const uint4 wb = *reinterpret_cast<const uint4*>(ra + 8 * 128 + 32 * ks);  // row g + 8
+      fd_mma<T>(c, wa.x, wb.x, wa.y, wb.y, qb[ks][0], qb[ks][1]);
+      fd_mma<T>(c, wa.z, wb.z, wa.w, wb.w, qb[ks][2], qb[ks][3]);
+    }
+    // c: rows g, g + 8 of the tile x heads 2t, 2t + 1
+    const int rr = tile_w * 16 + fg;
+    if (2 * ft < G) {
+      spart[half_w][rr][2 * ft] = c[0];
+      spart[half_w][rr + 8][2 * ft] = c[2];
+    }
+    if (2 * ft + 1 < G) {
+      spart[half_w][rr][2 * ft + 1] = c[1];
+      spart[half_w][rr + 8][2 * ft + 1] = c[3];
+    }
+    __syncthreads();
+    for (int idx = tid; idx < rows * G; idx += kFdThreads) {
+      const int r = idx / G, h = idx - r * G;
+      const float v = spart[0][r][h] + spart[1][r][h];
+      sc[h * p.cap + r0 + r] = DT<T>::from_f(round_to<T>(round_to<T>(v) * scale));
     }
     next(i);
   }

@@ -74,11 +74,11 @@ constexpr int kThreads = kWarps * 32;
 #ifndef IE_SK_MINBLOCKS_MT1
 #define IE_SK_MINBLOCKS_MT1 IE_SK_MINBLOCKS  // the same for M <= 8 (one n-tile of activation rows)
 #endif
-#ifndef IE_SK_EARLY_W
-#define IE_SK_EARLY_W 0  // 1: first weight batch requested before waiting for the previous kernel
-#endif
-#if IE_SK_EARLY_W && (IE_SK_PERSIST || !IE_SK_PIPE)
-#error "IE_SK_EARLY_W needs IE_SK_PIPE and no IE_SK_PERSIST"
+#ifndef IE_SK_EARLY_W_MAX_M
+// Launches with at most this many activation rows request their first weight
+// batch before waiting for the previous kernel (SkinnyParams::early_w).
+// Measured on the decode engine: +3 % at 1 row, -18 % at 8 rows.
+#define IE_SK_EARLY_W_MAX_M 2
 #endif
 constexpr int kWords = IE_SK_LOADW / 4;  // 32-bit words per lane per row per k-step
 constexpr int kStep = kWords * 2 * 4;    // k elements per step (4 lanes share a row)
@@ -392,12 +392,13 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? IE_SK_MINBLOCKS_MT1 : IE_S
   // Programmatic dependent launch: activations (X) come from the previous
   // kernel and the outputs may be buffers it still reads, so neither is
   // touched before this wait; the next kernel may be scheduled from here.
-  // With IE_SK_EARLY_W the first weight batch is requested before the wait
+  // With early_w the first weight batch is requested before the wait
   // (weights are never written by the kernels this one can overlap with).
-#if !IE_SK_EARLY_W
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-#endif
+  const bool early = !IE_SK_PERSIST && IE_SK_PIPE && p.early_w;
+  if (!early) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  }
 
 #if IE_SK_PERSIST
   for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
@@ -466,14 +467,12 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? IE_SK_MINBLOCKS_MT1 : IE_S
     {
       Batch<NMAT, MT> b0, b1;
       int s = s_begin;
-#if IE_SK_EARLY_W
       if (s < s_end) load_w(b0, s);
-      asm volatile("griddepcontrol.wait;" ::: "memory");
-      asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+      if (early) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+      }
       if (s < s_end) load_x(b0, s);
-#else
-      if (s < s_end) load(b0, s);
-#endif
       while (s < s_end) {
         if (s + kUnroll < s_end) load(b1, s + kUnroll);
         compute(b0);
@@ -679,6 +678,7 @@ static cudaError_t launch_skinny_t(const SkinnyParams& p0, int tiles, cudaStream
   p.w_wide = rows_wide(p.W0, p.ldw) && (nmat < 2 || rows_wide(p.W1, p.ldw)) &&
              (EPI != EPI_QKV || p.n_kv_heads == 0 || (rows_wide(p.W1, p.ldw) && rows_wide(p.W2, p.ldw)));
   p.x_wide = rows_wide(p.X, p.ldx);
+  p.early_w = p.M <= IE_SK_EARLY_W_MAX_M;
   if (p.M <= 8) return launch_variant<T, 1, EPI>(p, st);
   return launch_variant<T, 2, EPI>(p, st);
 }

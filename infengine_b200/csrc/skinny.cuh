@@ -37,6 +37,9 @@ struct SkinnyParams {
   int64_t ldw = 0;
   // set by launch_skinny: all weight / activation rows 32-byte aligned; tile count
   bool w_wide = false, x_wide = false;
+  // set by launch_skinny: first weight batch requested before the
+  // programmatic-launch wait (few activation rows)
+  bool early_w = false;
   int tiles = 0;
   void* Y = nullptr;
   int64_t ldy = 0;
