@@ -30,8 +30,10 @@
 
 // ------------------------------------------------ split-KV decode attention
 // Decode-time attention (a few query rows, each over its whole cache) spread
-// over the GPU: one thread-block cluster of kFdCluster CTAs per (query row,
-// KV head); CTA c of the cluster takes cache rows [c*len/8, (c+1)*len/8).
+// over the GPU: one thread-block cluster of C CTAs per (query row, KV head),
+// C = 16 when there are at most 8 (row, KV head) pairs (batch-1 decode, any
+// tensor-parallel split), else 8; CTA c of the cluster takes cache rows
+// [c*len/C, (c+1)*len/C).
 //  * Cache rows reach shared memory by untiled bulk copies
 //    (cp.async.bulk, 64 rows = 16 KB each) through a 6-deep ring completed on
 //    mbarriers, so a CTA keeps up to 96 KB of K/V in flight. Rows older than
@@ -58,7 +60,7 @@ __device__ int g_attn_status = 0;
 
 namespace {
 
-constexpr int kFdCluster = 8;
+constexpr int kFdClusterMax = 16;  // CTAs per cluster: 8, or 16 when few (row, head) pairs
 constexpr int kFdThreads = 256;
 constexpr int kFdWarps = kFdThreads / 32;
 constexpr int kFdRows = 64;
@@ -117,10 +119,11 @@ __device__ __forceinline__ void cluster_sync_all() {
 // The same shared-memory word of every CTA of the cluster (rank order). The
 // loads carry no memory clobber: they follow a cluster barrier and are all
 // issued before any is used.
-__device__ __forceinline__ void ld_cluster_all(const float* local, float (&v)[kFdCluster]) {
+template <int C>
+__device__ __forceinline__ void ld_cluster_all(const float* local, float (&v)[C]) {
   const uint32_t a = fd_smem_u32(local);
 #pragma unroll
-  for (unsigned r = 0; r < kFdCluster; ++r) {
+  for (unsigned r = 0; r < C; ++r) {
     uint32_t remote;
     asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(a), "r"(r));
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v[r]) : "r"(remote));
@@ -148,9 +151,8 @@ __device__ __forceinline__ uint32_t fd_pack2(float lo, float hi) {
   return (uint32_t)(*reinterpret_cast<uint16_t*>(&a)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&b)) << 16);
 }
 
-template <typename T, int G>
-__global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
-    decode_attention_kernel(const FdParams p) {
+template <typename T, int G, int C>
+__global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdParams p) {
   extern __shared__ __align__(128) unsigned char fd_smem[];
   __shared__ float qf[G][128];
   __shared__ float opart[G * 128];
@@ -177,8 +179,8 @@ __global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
   const bool bad = pos < 0 || pos >= p.cache_rows;
   if (bad && rank == 0 && tid == 0) atomicExch(&g_attn_status, IE_ERR_INVALID_ARG);
   const int len = bad ? 0 : pos + 1;
-  const int j0 = (int)((int64_t)len * rank / kFdCluster);
-  const int n = (int)((int64_t)len * (rank + 1) / kFdCluster) - j0;
+  const int j0 = (int)((int64_t)len * rank / C);
+  const int n = (int)((int64_t)len * (rank + 1) / C) - j0;
   const int nk = (n + kFdRows - 1) / kFdRows, total = 2 * nk;
   const int64_t base = (int64_t)(m / p.rows_per_seq) * p.cbs + (int64_t)hk * p.chs;
   const T* kh = static_cast<const T*>(p.kc) + base;
@@ -323,9 +325,9 @@ __global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
   cluster_sync_all();
   if (tid < G) {
     float v = -INFINITY;
-    float all[kFdCluster];
-    ld_cluster_all(&cmax[tid], all);
-    for (unsigned r = 0; r < kFdCluster; ++r) v = fmaxf(v, all[r]);
+    float all[C];
+    ld_cluster_all<C>(&cmax[tid], all);
+    for (unsigned r = 0; r < C; ++r) v = fmaxf(v, all[r]);
     gmax[tid] = v;
   }
   __syncthreads();
@@ -357,9 +359,9 @@ __global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
   cluster_sync_all();
   if (tid < G) {
     float v = 0.f;
-    float all[kFdCluster];
-    ld_cluster_all(&csum[tid], all);
-    for (unsigned r = 0; r < kFdCluster; ++r) v += all[r];
+    float all[C];
+    ld_cluster_all<C>(&csum[tid], all);
+    for (unsigned r = 0; r < C; ++r) v += all[r];
     ginv[tid] = 1.0f / v;
   }
   __syncthreads();
@@ -415,22 +417,22 @@ __global__ void __cluster_dims__(kFdCluster, 1, 1) __launch_bounds__(kFdThreads)
     opart[e] = s;
   }
   cluster_sync_all();
-  constexpr int kPer = G * 128 / kFdCluster;
+  constexpr int kPer = G * 128 / C;
   if (tid < kPer) {
     const int e = (int)rank * kPer + tid;
     float s = 0.f;
-    float all[kFdCluster];
-    ld_cluster_all(&opart[e], all);
-    for (unsigned r = 0; r < kFdCluster; ++r) s += all[r];
+    float all[C];
+    ld_cluster_all<C>(&opart[e], all);
+    for (unsigned r = 0; r < C; ++r) s += all[r];
     const int h = e >> 7, d = e & 127;
     static_cast<T*>(p.out)[(int64_t)m * p.ld_out + (int64_t)(hk * G + h) * 128 + d] = DT<T>::from_f(s);
   }
   cluster_sync_all();  // remote reads of opart are done before any CTA exits
 }
 
-template <typename T, int G>
+template <typename T, int G, int C>
 cudaError_t launch_decode_attention(const FdParams& p, int n_kv_heads, int R, cudaStream_t st) {
-  auto kernel = decode_attention_kernel<T, G>;
+  auto kernel = decode_attention_kernel<T, G, C>;
   const size_t smem = kFdRingBytes + (size_t)G * p.cap * sizeof(T);
   static size_t configured[64] = {};  // per device
   int dev = 0;
@@ -438,21 +440,39 @@ cudaError_t launch_decode_attention(const FdParams& p, int n_kv_heads, int R, cu
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (smem > configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess && C > 8) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
     configured[dev] = smem;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kFdCluster, n_kv_heads, R);
+  cfg.gridDim = dim3(C, n_kv_heads, R);
   cfg.blockDim = dim3(kFdThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   const char* env = getenv("IE_PDL");
-  cfg.numAttrs = (env && env[0] == '0') ? 0 : 1;
+  cfg.numAttrs = (env && env[0] == '0') ? 1 : 2;
   return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
+// Cluster size: 16 CTAs per (row, KV head) when there are few pairs, else 8.
+// Graph-timed at position 2048: 8 KV heads 9.3 -> 8.9 us, 1 KV head (8-way
+// tensor parallel) 8.8 -> 6.9 us; at 8191 23.7 -> 18.8 and 23.4 -> 14.4 us.
+// IE_FD_CLUSTER=8|16 in the environment forces one.
+int fd_cluster_size(int pairs) {
+  static const int forced = [] {
+    const char* e = getenv("IE_FD_CLUSTER");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced == 8 || forced == 16) return forced;
+  return pairs <= 8 ? 16 : 8;
 }
 
 }  // namespace
@@ -503,19 +523,24 @@ extern "C" int ie_attention_decode(ie_dtype dt, int R, int rows_per_seq, int n_q
   p.rows_per_seq = rows_per_seq;
   p.out = out;
   p.ld_out = ld_out;
-  p.cap = ((cache_rows + kFdCluster - 1) / kFdCluster + 7) / 8 * 8;
+  const int C = fd_cluster_size(n_kv_heads * R);
+  // score slots per head: the 8-CTA slice bound serves both cluster sizes
+  p.cap = ((cache_rows + 8 - 1) / 8 + 7) / 8 * 8;
   if (kFdRingBytes + (size_t)group * p.cap * 2 > 200 * 1024) return IE_ERR_UNSUPPORTED;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e;
-#define IE_FD(T)                                                                   \
-  switch (group) {                                                                 \
-    case 1: e = launch_decode_attention<T, 1>(p, n_kv_heads, R, st); break;        \
-    case 2: e = launch_decode_attention<T, 2>(p, n_kv_heads, R, st); break;        \
-    case 4: e = launch_decode_attention<T, 4>(p, n_kv_heads, R, st); break;        \
-    default: e = launch_decode_attention<T, 8>(p, n_kv_heads, R, st); break;       \
+#define IE_FD(T, CL)                                                                   \
+  switch (group) {                                                                     \
+    case 1: e = launch_decode_attention<T, 1, CL>(p, n_kv_heads, R, st); break;        \
+    case 2: e = launch_decode_attention<T, 2, CL>(p, n_kv_heads, R, st); break;        \
+    case 4: e = launch_decode_attention<T, 4, CL>(p, n_kv_heads, R, st); break;        \
+    default: e = launch_decode_attention<T, 8, CL>(p, n_kv_heads, R, st); break;       \
   }
-  if (dt == IE_DTYPE_F16) { IE_FD(__half) }
-  else { IE_FD(__nv_bfloat16) }
+  if (dt == IE_DTYPE_F16) {
+    if (C == 16) { IE_FD(__half, 16) } else { IE_FD(__half, 8) }
+  } else {
+    if (C == 16) { IE_FD(__nv_bfloat16, 16) } else { IE_FD(__nv_bfloat16, 8) }
+  }
 #undef IE_FD
   return e == cudaSuccess ? IE_OK : IE_ERR_LAUNCH;
 }
