@@ -45,6 +45,12 @@ def test_dropin_library_exports_reference_signatures(ie):
         "swiglu(int, __half*, __half*, __half*)",
         "lm_head(cublasContext*, int, __half*, __half*, __half*)",
         "sample_token_amax(__half const*, int*)",
+        "attn(cublasContext*, float const*, float const*, int, __half*, __half*, __half*, __half*, __half*, __half*, "
+        "void*, void*, int)",
+        "decode_attn(cublasContext*, float const*, float const*, int, __half*, __half*, __half*, __half*, __half*, "
+        "__half*, void*, void*, int)",
+        "attn_workspace_size(int)",
+        "kv_cache_size()",
     ):
         assert sig in out, sig
 
@@ -105,3 +111,29 @@ def test_python_mirror_fails_loudly_without_library(monkeypatch, ie, tmp_path):
     monkeypatch.setattr(ie, "_lib_handle", None)
     with pytest.raises(RuntimeError, match="missing"):
         ie.lib()
+
+
+def test_engine_and_loader_reject_bad_arguments_without_device(ie):
+    """Engine creation and the loader validate before any device work."""
+    lib = ie.lib()
+    vp = ctypes.c_void_p
+    out = vp()
+    from infengine_b200.engine import LlamaDesc, _bind
+    _bind()
+    # null descriptor
+    assert lib.ie_engine_create(1, None, 1, 128, 16, None, ctypes.byref(out)) == -1
+    # descriptor with missing weights
+    d = LlamaDesc()
+    d.n_layers, d.hidden, d.n_q_heads, d.n_kv_heads, d.head_dim, d.ffn_dim, d.vocab = 1, 256, 2, 1, 128, 512, 100
+    assert lib.ie_engine_create(1, ctypes.byref(d), 1, 128, 16, None, ctypes.byref(out)) == -1
+    assert not out.value
+    # engine calls on a null engine
+    assert lib.ie_engine_decode(None, 1, None) == -1
+    assert lib.ie_engine_step(None, None, None) == -1
+    # loader: missing file
+    from infengine_b200.loader import _bind as bind_loader
+    bind_loader()
+    arr = (ctypes.c_char_p * 1)(b"/nonexistent/model.safetensors")
+    assert lib.ie_llama_load(arr, 1, 1, 1, 0, 128, 1e-5, None, ctypes.byref(out)) == -1
+    # world / rank out of range
+    assert lib.ie_llama_load(arr, 1, 1, 2, 2, 128, 1e-5, None, ctypes.byref(out)) == -1
