@@ -29,7 +29,7 @@ CFLAGS = ARCH + [
 ]
 
 CORE_SOURCES = ["capi.cu", "skinny.cu", "gemm_tc.cu", "noalloc.cu", "comm.cu", "attention.cu", "p2p.cu", "norm.cu",
-                "engine.cu", "loader.cu"]
+                "engine.cu", "loader.cu", "attention_tc.cu"]
 DROPIN_SOURCES = ["dropin.cu"]
 
 LIB_CORE = PKG / "libinfengine_b200.so"

@@ -23,6 +23,7 @@
 //    after the p.V accumulation. Its outputs differ from the chain by about a
 //    rounding step of p.
 #include <climits>
+#include <cstring>
 #include <cstdlib>
 #include <type_traits>
 #include "ie_common.cuh"
@@ -31,9 +32,9 @@
 // ------------------------------------------------ split-KV decode attention
 // Decode-time attention (a few query rows, each over its whole cache) spread
 // over the GPU: one thread-block cluster of C CTAs per (query row, KV head),
-// C = 16 when there are at most 8 (row, KV head) pairs (batch-1 decode, any
-// tensor-parallel split), else 8; CTA c of the cluster takes cache rows
-// [c*len/C, (c+1)*len/C).
+// C = 16 for at most 4 KV heads, else 8, whatever the number of rows (so a
+// row's result does not depend on the batch); CTA c of the cluster takes
+// cache rows [c*len/C, (c+1)*len/C).
 //  * Cache rows reach shared memory by untiled bulk copies
 //    (cp.async.bulk, 64 rows = 16 KB each) through a 6-deep ring completed on
 //    mbarriers, so a CTA keeps up to 96 KB of K/V in flight. Rows older than
@@ -60,7 +61,6 @@ __device__ int g_attn_status = 0;
 
 namespace {
 
-constexpr int kFdClusterMax = 16;  // CTAs per cluster: 8, or 16 when few (row, head) pairs
 constexpr int kFdThreads = 256;
 constexpr int kFdWarps = kFdThreads / 32;
 constexpr int kFdRows = 64;
@@ -462,17 +462,22 @@ cudaError_t launch_decode_attention(const FdParams& p, int n_kv_heads, int R, cu
   return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
-// Cluster size: 16 CTAs per (row, KV head) when there are few pairs, else 8.
-// Graph-timed at position 2048: 8 KV heads 9.3 -> 8.9 us, 1 KV head (8-way
-// tensor parallel) 8.8 -> 6.9 us; at 8191 23.7 -> 18.8 and 23.4 -> 14.4 us.
-// IE_FD_CLUSTER=8|16 in the environment forces one.
-int fd_cluster_size(int pairs) {
+// Cluster size from the KV head count alone: 16 CTAs per (row, KV head) for
+// at most 4 KV heads (the tensor-parallel shards of an 8-head model), else 8.
+// The key slices and the order in which their partial sums meet follow from
+// the cluster size, so it must not depend on how many rows share a launch: a
+// row then gets the same bits alone, in a batch, or inside a verify block.
+// Graph-timed at position 2048, 8 -> 16 CTAs: 8 KV heads one row 9.3 -> 8.9 us
+// but 8 rows slower (batch-8 decode 5.18 ms a step with 16, about 4.8 with 8);
+// 1 KV head 8.8 -> 6.9 us; at 8191 23.4 -> 14.4 us.
+// IE_FD_CLUSTER=8|16 in the environment forces one (for measurements).
+int fd_cluster_size(int n_kv_heads) {
   static const int forced = [] {
     const char* e = getenv("IE_FD_CLUSTER");
     return e ? atoi(e) : 0;
   }();
   if (forced == 8 || forced == 16) return forced;
-  return pairs <= 8 ? 16 : 8;
+  return n_kv_heads <= 4 ? 16 : 8;
 }
 
 }  // namespace
@@ -523,7 +528,7 @@ extern "C" int ie_attention_decode(ie_dtype dt, int R, int rows_per_seq, int n_q
   p.rows_per_seq = rows_per_seq;
   p.out = out;
   p.ld_out = ld_out;
-  const int C = fd_cluster_size(n_kv_heads * R);
+  const int C = fd_cluster_size(n_kv_heads);
   // score slots per head: the 8-CTA slice bound serves both cluster sizes
   p.cap = ((cache_rows + 8 - 1) / 8 + 7) / 8 * 8;
   if (kFdRingBytes + (size_t)group * p.cap * 2 > 200 * 1024) return IE_ERR_UNSUPPORTED;
@@ -769,6 +774,15 @@ __global__ void __launch_bounds__(kPaThreads) prefill_attention_kernel(const PaP
   }
 }
 
+// The tcgen05 kernel unless IE_PREFILL_ATTN=mma selects the mma.sync one.
+bool use_tc_prefill() {
+  static const bool tc = [] {
+    const char* e = getenv("IE_PREFILL_ATTN");
+    return !(e && std::strcmp(e, "mma") == 0);
+  }();
+  return tc;
+}
+
 template <typename T>
 cudaError_t launch_prefill_attention(const PaParams& p, int n_q_heads, cudaStream_t st) {
   auto kernel = prefill_attention_kernel<T>;
@@ -816,6 +830,9 @@ extern "C" int ie_attention(ie_dtype dt, int S, int pos0, int n_q_heads, int n_k
     return ie_attention_decode(dt, S, S, n_q_heads, n_kv_heads, head_dim, q, q_head_stride, k_cache, v_cache,
                                cache_head_stride, 0, pos0 + S, nullptr, pos0, out, ld_out, stream);
   if ((int64_t)S > 65535LL * kPaRows || n_q_heads > 65535) return IE_ERR_UNSUPPORTED;
+  if (use_tc_prefill())
+    return launch_tc_attention(dt, S, pos0, n_q_heads, n_kv_heads, q, q_head_stride, k_cache, v_cache,
+                               cache_head_stride, out, ld_out, stream);
   PaParams p;
   p.q = q;
   p.q_head_stride = q_head_stride;

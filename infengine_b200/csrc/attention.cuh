@@ -8,4 +8,12 @@ namespace ie {
 // position was outside its cache. Returns the word; clears it when asked.
 int read_attn_status(bool clear);
 
+// Causal prefill attention on tcgen05 (attention_tc.cu), head_dim 128; the
+// arguments are ie_attention's after its checks. Returns an ie_status.
+int launch_tc_attention(ie_dtype dt, int S, int pos0, int n_q_heads, int n_kv_heads, const void* q,
+                        int64_t q_head_stride, const void* k_cache, const void* v_cache, int64_t cache_head_stride,
+                        void* out, int64_t ld_out, void* stream);
+// Status word of that kernel (IE_ERR_TIMEOUT when a bounded wait gave up).
+int read_tca_status(bool clear);
+
 }  // namespace ie

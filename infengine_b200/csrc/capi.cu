@@ -60,7 +60,8 @@ int ie_device_status(int clear) {
   const int b = read_skinny_status(clear != 0);
   const int c = read_attn_status(clear != 0);
   const int d = read_norm_status(clear != 0);
-  return a != IE_OK ? a : (b != IE_OK ? b : (c != IE_OK ? c : d));
+  const int e = read_tca_status(clear != 0);
+  return a != IE_OK ? a : (b != IE_OK ? b : (c != IE_OK ? c : (d != IE_OK ? d : e)));
 }
 
 static int gemm_store(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw,

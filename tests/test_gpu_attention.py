@@ -11,7 +11,8 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 @pytest.mark.parametrize("S,pos0,nq,nkv", [(1, 0, 32, 8), (1, 300, 32, 8), (37, 0, 32, 8), (16, 50, 8, 2),
                                            (5, 2043, 4, 1), (17, 0, 8, 2), (64, 0, 8, 2), (65, 3, 8, 2),
-                                           (300, 100, 32, 8), (1024, 0, 8, 2)])
+                                           (300, 100, 32, 8), (1024, 0, 8, 2), (129, 0, 4, 4), (200, 1900, 8, 2),
+                                           (2048, 64, 8, 1)])
 def test_attention_core(ie, cuda, dt, S, pos0, nq, nkv):
     """S <= 16: split-KV kernel; S > 16: tensor-core flash kernel (chunked
     prefill when pos0 > 0; ragged last query and key blocks)."""
@@ -25,6 +26,7 @@ def test_attention_core(ie, cuda, dt, S, pos0, nq, nkv):
     out = cuda.full((S, nq * 128), float("nan"), dtype=torch_dtype(dt), device="cuda")
     ie.attention(to_dev(q, dt), to_dev(k, dt), to_dev(v, dt), out, pos0, n_kv_heads=nkv)
     got = from_dev(out)
+    assert ie.device_status() == 0
     want = oracle.attention(q, k, v, pos0, dt)
     assert not np.isnan(got).any()
     # a rounding flip of one probability moves an output by about one p-ulp
@@ -85,6 +87,27 @@ def test_attention_decode_batched_and_verify(ie, cuda, dt):
     ie.attention_decode(to_dev(qv, dt), to_dev(k[0], dt), to_dev(v[0], dt), outv, pos0=900, rows_per_seq=5)
     assert ie.device_status() == 0
     _check_close(from_dev(outv), oracle.attention(qv, k[0], v[0], 900, dt), dt)
+
+
+@pytest.mark.parametrize("nq,nkv", [(32, 8), (8, 2)])
+def test_attention_decode_batch_invariant(ie, cuda, nq, nkv):
+    """A row gets the same bits alone as inside a batch of four (the key split
+    and the order of the partial sums do not depend on the batch)."""
+    dt = "bf16"
+    rng = np.random.default_rng(11)
+    B, rows = 4, 2048
+    pos = np.array([2047, 5, 700, 1500], dtype=np.int32)
+    q = oracle.round_dt(rng.standard_normal((nq, B, 128), dtype=np.float32), dt)
+    k = to_dev(oracle.round_dt(rng.standard_normal((B, nkv, rows, 128), dtype=np.float32), dt), dt)
+    v = to_dev(oracle.round_dt(rng.standard_normal((B, nkv, rows, 128), dtype=np.float32), dt), dt)
+    out = cuda.empty((B, nq * 128), dtype=torch_dtype(dt), device="cuda")
+    ie.attention_decode(to_dev(q, dt), k, v, out, positions=cuda.from_numpy(pos).cuda())
+    for b in range(B):
+        one = cuda.empty((1, nq * 128), dtype=torch_dtype(dt), device="cuda")
+        ie.attention_decode(to_dev(np.ascontiguousarray(q[:, b:b + 1]), dt), k[b:b + 1], v[b:b + 1], one,
+                            positions=cuda.from_numpy(pos[b:b + 1]).cuda())
+        assert cuda.equal(one[0], out[b]), b
+    assert ie.device_status() == 0
 
 
 def test_attention_decode_bad_position(ie, cuda):
