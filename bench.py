@@ -505,6 +505,17 @@ def single_case(torch, name: str, steps: int, seed: int):
         torch.cuda.synchronize()
         print(json.dumps({"case": name, "layers": n_layers, "decode_steps": steps}))
         return
+    elif name == "prefill_attention":
+        # the attention core of a 2048-token prefill: causal 2048 x 2048, 32
+        # query / 8 KV heads (K/V of one layer: 8 MB, L2-resident like in the
+        # engine, where the QKV projection has just written them)
+        S = PROMPT
+        q = torch.randn(NQ, S, HD, generator=g, device=dev, dtype=torch.float32).to(bf)
+        kc = torch.randn(NKV, S, HD, generator=g, device=dev, dtype=torch.float32).to(bf)
+        vc = torch.randn(NKV, S, HD, generator=g, device=dev, dtype=torch.float32).to(bf)
+        out = torch.empty(S, NQ * HD, device=dev, dtype=bf)
+        fn = lambda: ie.attention(q, kc, vc, out, 0, n_kv_heads=NKV)
+        flops = 4.0 * NQ * HD * S * (S + 1) / 2
     elif name.startswith("prefill_"):
         S = 2048
         xs = torch.randn(S, H, generator=g, device=dev, dtype=torch.float32).to(bf)
@@ -529,10 +540,19 @@ def single_case(torch, name: str, steps: int, seed: int):
             raise SystemExit(f"unknown case {name}")
     else:
         raise SystemExit(f"unknown case {name}")
+    fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
     for _ in range(steps):
         fn()
+    e1.record()
     torch.cuda.synchronize()
-    print(json.dumps({"case": name, "launches": steps}))
+    us = e0.elapsed_time(e1) * 1e3 / max(steps, 1)
+    res = {"case": name, "launches": steps + 1, "us_per_launch": round(us, 2)}
+    if name == "prefill_attention":
+        res["tflops"] = round(flops / us / 1e6, 1)
+    print(json.dumps(res))
 
 
 # ------------------------------------------------ full model through the engine
@@ -621,7 +641,8 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", default=None,
-                    help="for profiling: one kernel (gate_up|down|o|qkv|lm_head|prefill_{qkv,o,gate_up,down}) "
+                    help="for profiling: one kernel (gate_up|down|o|qkv|lm_head|prefill_{qkv,o,gate_up,down}|"
+                         "prefill_attention) "
                          "--steps times, or the engine (engine_decode: 32 layers, engine_small: 2 layers) with a "
                          "2048-token prefill and --steps decode steps")
     args = ap.parse_args()

@@ -5,21 +5,29 @@
 // over the key blocks, so that the softmax uses the exact row maximum the
 // reference uses (kernels/softmax.cu:55-103) and never rescales an
 // accumulator:
-//   pass 1: S = Q K^T (tcgen05.mma 128x128x128, fp32 in TMEM) ->
-//           t = round(round(s) * rsqrt(128)), causal mask -> row max m;
-//   pass 2: S again -> e = exp(t - m) (fp32, summed into l), p = round(e)
+//   pass 1: S = Q K^T (tcgen05.mma 128x128x128, fp32 in TMEM) -> the row
+//           maximum of the raw scores over the causal keys; rounding and the
+//           positive scale are monotone, so max t = round(round(max s) * scale)
+//           for t = round(round(s) * rsqrt(128));
+//   pass 2: S again -> t -> e = exp(t - m) (fp32, summed into l), p = round(e)
 //           written to shared memory as the A operand -> O += P V
 //           (tcgen05.mma, V as an MN-major operand straight from its TMA tile);
 //   out = round(O / l).
-// The reference rounds p after the division by the sum; here the division
-// follows the P.V accumulation, so outputs differ from the chain by about a
-// rounding step of p (tests bound it).
+// exp is 2^(t*log2(e) - m*log2(e)) on the special-function unit (ex2.approx,
+// relative error about 2^-22, plus one fp32 rounding of the exponent), where
+// the reference calls expf; the reference also rounds p after the division
+// by the sum, while here the division follows the P.V accumulation. Outputs
+// therefore differ from the chain by about a rounding step of p (tests bound
+// it). Deterministic: no atomics, fixed summation order.
 //
-// Warp roles (192 threads): warp 0 = TMA producer (Q once, then the key /
-// value tiles in the order the MMAs use them through a 3-stage ring), warp 1 =
+// Warp roles (320 threads): warp 0 = TMA producer (Q once, then the key /
+// value tiles in the order the MMAs use them through a 4-stage ring), warp 1 =
 // MMA issuer (one elected thread; TMEM: two S buffers of 128 columns, O in 128
-// more), warps 2-5 = softmax and epilogue, one query row per thread (TMEM lane
-// = row). The next block's scores are computed while the softmax works on the
+// more), warps 2-9 = softmax and epilogue: TMEM lane = query row, warp w takes
+// lane quarter w & 3 and key half (w - 2) >> 2 of each block, so two warps per
+// scheduler hide each other's latency; the halves of a row meet once, in
+// shared memory, for the row maximum and for the sum. P is double-buffered
+// and the next block's scores are computed while the softmax works on the
 // current one. Every mbarrier wait is bounded (2 s): on expiry IE_ERR_TIMEOUT
 // is recorded, every role leaves its loop, the MMAs and copies in flight are
 // drained and the TMEM is freed before the CTA exits.
@@ -38,7 +46,7 @@ namespace {
 using namespace tc;
 
 constexpr int kBM = 128, kBN = 128, kD = 128;
-constexpr int kStages = 3;
+constexpr int kStages = 4;
 constexpr int kTile = kBN * kD * 2;    // one K or V tile: two 64-column boxes, 32 KB
 constexpr int kHalf = kTile / 2;       // 16 KB
 constexpr int kQBytes = kBM * kD * 2;  // 32 KB
@@ -52,6 +60,7 @@ constexpr int kOffP = kQBytes, kOffRing = kQBytes + 2 * kPBytes;
 constexpr int kOffRed = kOffRing + kStages * kTile;
 constexpr int kOffBars = kOffRed + 2 * kBM * 4;
 constexpr int kSmem = kOffBars + 256 + 1024;  // + alignment slack
+static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
 
 struct TcaArgs {
   CUtensorMap tmQ, tmK, tmV;  // 3-D (dim, row, head), boxes 64 x 128 x 1, 128-byte swizzle
@@ -118,8 +127,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
-  // bars: full[3] empty[3] q_full s_full[2] s_empty[2] p_full[2] p_empty[2] o_full drain
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 18);
+  // bars: full[kStages] empty[kStages] q_full s_full[2] s_empty[2] p_full[2]
+  // p_empty[2] o_full drain
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   int* issued_p = reinterpret_cast<int*>(tmem_holder + 2);
 
@@ -131,14 +141,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
   const int nkb = last_pos / kBN + 1;  // key blocks this query block needs
   const int n_tiles = 3 * nkb;         // pass 1: K; pass 2: K, V per block
 
+  constexpr int kB = 2 * kStages;  // barriers after the ring's full / empty pairs
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
-  auto empty_bar = [&](int s) { return smem_u32(bars + 3 + s); };
-  const uint32_t q_full = smem_u32(bars + 6);
-  auto s_full = [&](int b) { return smem_u32(bars + 7 + b); };
-  auto s_empty = [&](int b) { return smem_u32(bars + 9 + b); };
-  auto p_full = [&](int b) { return smem_u32(bars + 11 + b); };
-  auto p_empty = [&](int b) { return smem_u32(bars + 13 + b); };
-  const uint32_t o_full = smem_u32(bars + 15), drain_bar = smem_u32(bars + 16);
+  auto empty_bar = [&](int s) { return smem_u32(bars + kStages + s); };
+  const uint32_t q_full = smem_u32(bars + kB);
+  auto s_full = [&](int b) { return smem_u32(bars + kB + 1 + b); };
+  auto s_empty = [&](int b) { return smem_u32(bars + kB + 3 + b); };
+  auto p_full = [&](int b) { return smem_u32(bars + kB + 5 + b); };
+  auto p_empty = [&](int b) { return smem_u32(bars + kB + 7 + b); };
+  const uint32_t o_full = smem_u32(bars + kB + 9), drain_bar = smem_u32(bars + kB + 10);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -173,14 +184,23 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  // tile t of the producer order: pass 1 K_0..K_{n-1}; pass 2 K_0, V_0, K_1, V_1, ...
+  // Tile t, in the order the MMAs consume them (so the ring's lookahead is
+  // kStages tiles of that order): pass 1 K_0 .. K_{n-1}; pass 2 K_0, then
+  // K_{j+1}, V_j for j = 0 .. n-2, then V_{n-1}.
   auto tile_kind = [&](int t, int& kb, bool& is_v) {
-    if (t < nkb) {
+    const int u = t - nkb;
+    if (u < 0) {
       kb = t;
       is_v = false;
+    } else if (u == 0) {
+      kb = 0;
+      is_v = false;
+    } else if (u == 2 * nkb - 1) {
+      kb = nkb - 1;
+      is_v = true;
     } else {
-      kb = (t - nkb) >> 1;
-      is_v = ((t - nkb) & 1) != 0;
+      is_v = (u & 1) == 0;
+      kb = is_v ? u / 2 - 1 : (u + 1) / 2;
     }
   };
 
@@ -256,8 +276,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
       for (int kb = 0; ok && kb < nkb; ++kb) ok = qk(kb);  // pass 1
       if (ok) ok = qk(nkb);                                 // pass 2, block 0 scores
       for (int kb = 0; ok && kb < nkb; ++kb) {
-        if (kb + 1 < nkb) ok = qk(nkb + 2 * (kb + 1));      // next block's scores first
-        if (ok) ok = pv(nkb + 2 * kb + 1, kb);
+        if (kb + 1 < nkb) ok = qk(nkb + 2 * kb + 1);        // next block's scores first
+        if (ok) ok = pv(kb + 1 < nkb ? nkb + 2 * kb + 2 : 3 * nkb - 1, kb);
       }
       if (ok) mma_commit(o_full);
       if (*abort_flag && issued_any) {
