@@ -10,8 +10,7 @@
 //           positive scale are monotone, so max t = round(round(max s) * scale)
 //           for t = round(round(s) * rsqrt(128));
 //   pass 2: S again -> t -> e = exp(t - m) (fp32, summed into l), p = round(e)
-//           written to shared memory as the A operand -> O += P V
-//           (tcgen05.mma, V as an MN-major operand straight from its TMA tile);
+//           -> O += P V;
 //   out = round(O / l).
 // exp is 2^(t*log2(e) - m*log2(e)) on the special-function unit (ex2.approx,
 // relative error about 2^-22, plus one fp32 rounding of the exponent), where
@@ -20,17 +19,27 @@
 // therefore differ from the chain by about a rounding step of p (tests bound
 // it). Deterministic: no atomics, fixed summation order.
 //
-// Warp roles (320 threads): warp 0 = TMA producer (Q once, then the key /
-// value tiles in the order the MMAs use them through a 4-stage ring), warp 1 =
-// MMA issuer (one elected thread; TMEM: two S buffers of 128 columns, O in 128
-// more), warps 2-9 = softmax and epilogue: TMEM lane = query row, warp w takes
-// lane quarter w & 3 and key half (w - 2) >> 2 of each block, so two warps per
-// scheduler hide each other's latency; the halves of a row meet once, in
-// shared memory, for the row maximum and for the sum. P is double-buffered
-// and the next block's scores are computed while the softmax works on the
-// current one. Every mbarrier wait is bounded (2 s): on expiry IE_ERR_TIMEOUT
-// is recorded, every role leaves its loop, the MMAs and copies in flight are
-// drained and the TMEM is freed before the CTA exits.
+// Operands. The A operands live in tensor memory, so shared memory only holds
+// K and V (its bandwidth, shared by the TMA writes and the tensor cores'
+// operand reads, is what limits this kernel): Q is copied once into TMEM
+// columns [384, 448) (row = lane, two 16-bit values per 32-bit column, the
+// lower-indexed one in the low half), and each P block is written by the
+// softmax into the S buffer it was computed from — key half k of the row
+// into the first 32 columns of the 64 it read, so the two warps that share a
+// row never touch each other's columns. K is the K-major B operand of Q K^T,
+// V the MN-major B operand of P V straight from its TMA tile (no transpose).
+// TMEM: S0 [0,128), S1 [128,256), O [256,384), Q [384,448).
+//
+// Warp roles (320 threads): warp 0 = TMA producer (the K / V tiles in the
+// order the MMAs use them, through a 6-stage ring), warp 1 = MMA issuer (one
+// elected thread), warps 2-9 = softmax and epilogue: TMEM lane = query row,
+// warp w reads lane quarter w & 3 and key half (w - 2) >> 2 of each block, so
+// each scheduler holds two of them; the halves of a row meet once, in shared
+// memory, for the row maximum and for the sum. An S buffer is released by
+// the softmax warps in pass 1 (after they loaded it) and by the commit of the
+// P.V that read its P in pass 2. Every mbarrier wait is bounded (2 s): on
+// expiry IE_ERR_TIMEOUT is recorded, every role leaves its loop, the MMAs and
+// copies in flight are drained and the TMEM is freed before the CTA exits.
 #include <cstdio>
 #include <cstring>
 #include "ie_common.cuh"
@@ -46,24 +55,26 @@ namespace {
 using namespace tc;
 
 constexpr int kBM = 128, kBN = 128, kD = 128;
-constexpr int kStages = 4;
-constexpr int kTile = kBN * kD * 2;    // one K or V tile: two 64-column boxes, 32 KB
-constexpr int kHalf = kTile / 2;       // 16 KB
-constexpr int kQBytes = kBM * kD * 2;  // 32 KB
-constexpr int kPBytes = kBM * kBN * 2; // 32 KB per P buffer (two)
+constexpr int kStages = 6;
+constexpr int kTile = kBN * kD * 2;          // one K or V tile: two 64-column boxes, 32 KB
+constexpr int kHalf = kTile / 2;             // 16 KB
 constexpr int kSoftThreads = 256;            // 8 softmax / epilogue warps
 constexpr int kThreads = 64 + kSoftThreads;  // + TMA warp + MMA warp
-constexpr uint32_t kTmemCols = 512;    // S0 [0,128), S1 [128,256), O [256,384)
+constexpr int kSBufs = 2;                    // S (then P) buffers in TMEM
+constexpr int kOCol = kSBufs * kBN;          // O accumulator columns [256, 384)
+constexpr int kQCol = kOCol + kD;            // Q (A operand of Q K^T), 64 columns
+constexpr uint32_t kTmemCols = 512;
 constexpr unsigned long long kWaitNs = 2000000000ull;
-// smem: Q | P0 P1 | ring | cross-half row exchange | barriers
-constexpr int kOffP = kQBytes, kOffRing = kQBytes + 2 * kPBytes;
-constexpr int kOffRed = kOffRing + kStages * kTile;
+// smem: K/V ring | cross-half row exchange | barriers
+constexpr int kOffRed = kStages * kTile;
 constexpr int kOffBars = kOffRed + 2 * kBM * 4;
 constexpr int kSmem = kOffBars + 256 + 1024;  // + alignment slack
 static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
 
 struct TcaArgs {
-  CUtensorMap tmQ, tmK, tmV;  // 3-D (dim, row, head), boxes 64 x 128 x 1, 128-byte swizzle
+  CUtensorMap tmK, tmV;  // 3-D (dim, row, head), boxes 64 x 128 x 1, 128-byte swizzle
+  const void* q;         // [heads][S][128]
+  int64_t q_head_stride;
   int S, pos0, group;
   float scale;
   void* out;
@@ -122,20 +133,45 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
   for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 consecutive 32-bit TMEM columns of this warp's 32 lanes from registers;
+// waits until the stores are done.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+// D (TMEM) (+)= A (TMEM, K-major) . B (shared memory descriptor)
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                       uint32_t accum) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_constant__ TcaArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
-  // bars: full[kStages] empty[kStages] q_full s_full[2] s_empty[2] p_full[2]
-  // p_empty[2] o_full drain
+  // bars: full[kStages] empty[kStages] q_full s_full[2] s_rel_sm[2] s_rel_mma[2]
+  // p_full[2] o_full drain
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   int* issued_p = reinterpret_cast<int*>(tmem_holder + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qb = gridDim.x - 1 - blockIdx.x;  // heaviest (causal) blocks first
-  const int h = blockIdx.y, hk = h / a.group;
+  // grid (query heads, query blocks): the hardware starts CTAs in linear
+  // order, so the heaviest (causal) query blocks go first
+  const int qb = gridDim.y - 1 - blockIdx.y;
+  const int h = blockIdx.x, hk = h / a.group;
   const int q0 = qb * kBM;
   const int last_pos = a.pos0 + min(q0 + kBM, a.S) - 1;
   const int nkb = last_pos / kBN + 1;  // key blocks this query block needs
@@ -146,9 +182,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
   auto empty_bar = [&](int s) { return smem_u32(bars + kStages + s); };
   const uint32_t q_full = smem_u32(bars + kB);
   auto s_full = [&](int b) { return smem_u32(bars + kB + 1 + b); };
-  auto s_empty = [&](int b) { return smem_u32(bars + kB + 3 + b); };
-  auto p_full = [&](int b) { return smem_u32(bars + kB + 5 + b); };
-  auto p_empty = [&](int b) { return smem_u32(bars + kB + 7 + b); };
+  auto s_rel_sm = [&](int b) { return smem_u32(bars + kB + 3 + b); };   // pass 1: softmax read S
+  auto s_rel_mma = [&](int b) { return smem_u32(bars + kB + 5 + b); };  // pass 2: P.V read P
+  auto p_full = [&](int b) { return smem_u32(bars + kB + 7 + b); };
   const uint32_t o_full = smem_u32(bars + kB + 9), drain_bar = smem_u32(bars + kB + 10);
 
   if (threadIdx.x == 0) {
@@ -156,12 +192,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
-    mbar_init(q_full, 1);
-    for (int b = 0; b < 2; ++b) {
+    mbar_init(q_full, kSoftThreads / 32);
+    for (int b = 0; b < kSBufs; ++b) {
       mbar_init(s_full(b), 1);
-      mbar_init(s_empty(b), kSoftThreads / 32);
+      mbar_init(s_rel_sm(b), kSoftThreads / 32);
+      mbar_init(s_rel_mma(b), 1);
       mbar_init(p_full(b), kSoftThreads / 32);
-      mbar_init(p_empty(b), 1);
     }
     mbar_init(o_full, 1);
     mbar_init(drain_bar, 1);
@@ -186,7 +222,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
 
   // Tile t, in the order the MMAs consume them (so the ring's lookahead is
   // kStages tiles of that order): pass 1 K_0 .. K_{n-1}; pass 2 K_0, then
-  // K_{j+1}, V_j for j = 0 .. n-2, then V_{n-1}.
+  // K_{j+1}, V_j for j = 0 .. n-2, then V_{n-1} (the next block's scores are
+  // computed before the current block's P.V).
   auto tile_kind = [&](int t, int& kb, bool& is_v) {
     const int u = t - nkb;
     if (u < 0) {
@@ -207,10 +244,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------ TMA producer
-      const uint32_t sq = smem_u32(smem);
-      mbar_expect_tx(q_full, kQBytes);
-      tma_load_3d(sq, &a.tmQ, q_full, 0, q0, h);
-      tma_load_3d(sq + kHalf, &a.tmQ, q_full, 64, q0, h);
       int issued = 0;
       for (int t = 0; t < n_tiles && !*abort_flag; ++t) {
         const int s = t % kStages;
@@ -218,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
         int kb;
         bool is_v;
         tile_kind(t, kb, is_v);
-        const uint32_t dst = smem_u32(smem + kOffRing + s * kTile);
+        const uint32_t dst = smem_u32(smem + s * kTile);
         const CUtensorMap* map = is_v ? &a.tmV : &a.tmK;
         mbar_expect_tx(full_bar(s), kTile);
         tma_load_3d(dst, map, full_bar(s), 0, kb * kBN, hk);
@@ -232,52 +265,60 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
     if (lane == 0) {
       // ------------------------------------------------ MMA issuer
       const uint32_t id_qk = idesc_f16<T>(kBM, kBN, 0), id_pv = idesc_f16<T>(kBM, kD, 1);
-      const uint32_t sq = smem_u32(smem), sp = smem_u32(smem + kOffP);
       bool ok = wait(q_full, 0, abort_flag);
       fence_after();
       int sidx = 0;
       bool issued_any = false;
-      // S = Q . K_kb^T into S buffer sidx & 1 (tile t)
+      // S = Q . K_kb^T into S buffer sidx & 1 (tile t). The buffer's previous
+      // use (sidx - 2) was released by the softmax (pass 1) or by a P.V.
       auto qk = [&](int t) -> bool {
-        const int b = sidx & 1;
-        if (!wait(s_empty(b), (uint32_t)(((sidx >> 1) & 1) ^ 1), abort_flag)) return false;
+        const int b = sidx & 1, prev = sidx - 2;
+        if (prev >= 0) {
+          bool w;
+          if (prev < nkb) {
+            w = wait(s_rel_sm(b), (uint32_t)((prev >> 1) & 1), abort_flag);
+          } else {
+            const int first = nkb + ((b - nkb) & 1);  // first pass-2 use of buffer b
+            w = wait(s_rel_mma(b), (uint32_t)(((prev - first) >> 1) & 1), abort_flag);
+          }
+          if (!w) return false;
+        }
         const int s = t % kStages;
         if (!wait(full_bar(s), (uint32_t)((t / kStages) & 1), abort_flag)) return false;
         fence_after();
-        const uint32_t sk = smem_u32(smem + kOffRing + s * kTile);
+        const uint32_t sk = smem_u32(smem + s * kTile);
 #pragma unroll
-        for (int k = 0; k < kD / 16; ++k) {
-          const uint32_t off = (uint32_t)(k >> 2) * kHalf;
-          mma_f16(tmem + b * kBN, sw128_desc(sq + off) + 2 * (k & 3), sw128_desc(sk + off) + 2 * (k & 3), id_qk,
-                  k != 0 ? 1u : 0u);
-        }
+        for (int k = 0; k < kD / 16; ++k)
+          mma_ts(tmem + b * kBN, tmem + kQCol + 8 * k, sw128_desc(sk + (uint32_t)(k >> 2) * kHalf) + 2 * (k & 3),
+                 id_qk, k != 0 ? 1u : 0u);
         mma_commit(empty_bar(s));
         mma_commit(s_full(b));
         issued_any = true;
         ++sidx;
         return true;
       };
-      // O += P . V_kb (tile t; P buffer kb & 1)
+      // O += P_kb . V_kb (tile t); P_kb sits in the S buffer of pass-2 block kb
       auto pv = [&](int t, int kb) -> bool {
         if (!wait(p_full(kb & 1), (uint32_t)((kb >> 1) & 1), abort_flag)) return false;
         const int s = t % kStages;
         if (!wait(full_bar(s), (uint32_t)((t / kStages) & 1), abort_flag)) return false;
         fence_after();
-        const uint32_t sv = smem_u32(smem + kOffRing + s * kTile), spb = sp + (uint32_t)(kb & 1) * kPBytes;
+        const int b = (nkb + kb) & 1;
+        const uint32_t sv = smem_u32(smem + s * kTile);
 #pragma unroll
         for (int k = 0; k < kBN / 16; ++k)
-          mma_f16(tmem + 2 * kBN, sw128_desc(spb + (uint32_t)(k >> 2) * kHalf) + 2 * (k & 3),
-                  sw128_desc_mn(sv + (uint32_t)k * 16 * 128, kHalf), id_pv, (kb | k) != 0 ? 1u : 0u);
+          mma_ts(tmem + kOCol, tmem + b * kBN + 64 * (k >> 2) + 8 * (k & 3),
+                 sw128_desc_mn(sv + (uint32_t)k * 16 * 128, kHalf), id_pv, (kb | k) != 0 ? 1u : 0u);
         mma_commit(empty_bar(s));
-        mma_commit(p_empty(kb & 1));
+        mma_commit(s_rel_mma(b));
         issued_any = true;
         return true;
       };
-      for (int kb = 0; ok && kb < nkb; ++kb) ok = qk(kb);  // pass 1
-      if (ok) ok = qk(nkb);                                 // pass 2, block 0 scores
-      for (int kb = 0; ok && kb < nkb; ++kb) {
-        if (kb + 1 < nkb) ok = qk(nkb + 2 * kb + 1);        // next block's scores first
-        if (ok) ok = pv(kb + 1 < nkb ? nkb + 2 * kb + 2 : 3 * nkb - 1, kb);
+      for (int t = 0; ok && t < n_tiles; ++t) {  // the producer's order
+        int kb;
+        bool is_v;
+        tile_kind(t, kb, is_v);
+        ok = is_v ? pv(t, kb) : qk(t);
       }
       if (ok) mma_commit(o_full);
       if (*abort_flag && issued_any) {
@@ -298,7 +339,29 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
     const int qpos = a.pos0 + q0 + row;
     const uint32_t tlane = (uint32_t)(quad * 32) << 16;
     float* red = reinterpret_cast<float*>(smem + kOffRed);  // [2][128] cross-half exchange
-    uint8_t* const sp0 = smem + kOffP;
+    // Q row (this half's 64 dimensions) into TMEM; rows past S are zero
+    {
+      uint32_t w[32];
+      if (q0 + row < a.S) {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + (int64_t)h * a.q_head_stride +
+                                                          (int64_t)(q0 + row) * kD + half * 64);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint4 x = __ldg(src + j);
+          w[4 * j] = x.x;
+          w[4 * j + 1] = x.y;
+          w[4 * j + 2] = x.z;
+          w[4 * j + 3] = x.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) w[j] = 0u;
+      }
+      tmem_st32(tmem + tlane + kQCol + half * 32, w);
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_full);
+    }
     int sidx = 0;
     bool ok = true;
     // pass 1: the row maximum of the raw scores over the causal keys. Rounding
@@ -312,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
       tmem_ld64(tmem + tlane + b * kBN + half * 64, v);
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty(b));
+      if (lane == 0) mbar_arrive(s_rel_sm(b));
       ++sidx;
       const int lim = qpos - (kb * kBN + half * 64);  // keys i <= lim are visible
       if (lim >= 63) {
@@ -341,17 +404,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
     constexpr float kLog2e = 1.4426950408889634f;
     const float mb = -m * kLog2e;
     float l0 = 0.f, l1 = 0.f;
-    // pass 2: p = round(e) into shared memory for P.V
+    // pass 2: p = round(e) into the first 32 columns of this half's 64
     for (int kb = 0; ok && kb < nkb; ++kb) {
       const int b = sidx & 1;
-      if (!wait(p_empty(kb & 1), (uint32_t)(((kb >> 1) & 1) ^ 1), abort_flag)) { ok = false; break; }
       if (!wait(s_full(b), (uint32_t)((sidx >> 1) & 1), abort_flag)) { ok = false; break; }
       fence_after();
       float v[64];
       tmem_ld64(tmem + tlane + b * kBN + half * 64, v);
-      fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty(b));
       ++sidx;
       const int lim = qpos - (kb * kBN + half * 64);
       uint32_t pk[32];
@@ -368,15 +427,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
         l1 += e1;
         pk[i >> 1] = pack2_rn<T>(e0, e1);
       }
-      // keys half*64 .. +63 of this row: atom `half` of the K-major
-      // 128-byte-swizzled P tile, chunk j = keys 8j .. 8j+7
-      uint8_t* const dst = sp0 + (kb & 1) * kPBytes + half * kHalf + row * 128;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        *reinterpret_cast<uint4*>(dst + ((j ^ (row & 7)) << 4)) =
-            make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-      // P is read by the tensor cores (async proxy): make the stores visible
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tmem_st32(tmem + tlane + b * kBN + half * 64, pk);
+      fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full(kb & 1));
     }
@@ -389,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
       fence_after();
       const float inv = 1.0f / l;
       float v[64];
-      tmem_ld64(tmem + tlane + 2 * kBN + half * 64, v);
+      tmem_ld64(tmem + tlane + kOCol + half * 64, v);
       if (q0 + row < a.S) {
         T* orow = static_cast<T*>(a.out) + (int64_t)(q0 + row) * a.ld_out + (int64_t)h * kD + half * 64;
 #pragma unroll
@@ -410,11 +462,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
   __syncthreads();
   fence_after();
   if (*abort_flag && threadIdx.x == 0) {
-    // copies still in flight land before the CTA exits: Q and the last
-    // kStages tiles (an earlier tile's stage was reused, so it had landed)
-    const unsigned long long tq = globaltimer();
-    while (!mbar_try(q_full, 0) && globaltimer() - tq < kWaitNs / 4) {
-    }
+    // copies still in flight land before the CTA exits: the last kStages
+    // tiles (an earlier tile's stage was reused, so it had landed)
     const int issued = *issued_p;
     for (int t = max(0, issued - kStages); t < issued; ++t) {
       const unsigned long long t0 = globaltimer();
@@ -455,7 +504,7 @@ int launch(const TcaArgs& a, int n_q_heads, cudaStream_t st) {
     configured[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.S + kBM - 1) / kBM, n_q_heads);
+  cfg.gridDim = dim3(n_q_heads, (a.S + kBM - 1) / kBM);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmem;
   cfg.stream = st;
@@ -482,10 +531,12 @@ int launch_tc_attention(ie_dtype dt, int S, int pos0, int n_q_heads, int n_kv_he
   memset(&a, 0, sizeof(a));
   const int64_t rows = cache_head_stride / kD;
   if (rows > 0x7fffffff || S <= 0) return IE_ERR_UNSUPPORTED;
-  if (!make_map3(&a.tmQ, dt, q, S, n_q_heads, q_head_stride) ||
-      !make_map3(&a.tmK, dt, k_cache, (int)rows, n_kv_heads, cache_head_stride) ||
+  if ((S + kBM - 1) / kBM > 65535) return IE_ERR_UNSUPPORTED;
+  if (!make_map3(&a.tmK, dt, k_cache, (int)rows, n_kv_heads, cache_head_stride) ||
       !make_map3(&a.tmV, dt, v_cache, (int)rows, n_kv_heads, cache_head_stride))
     return IE_ERR_UNSUPPORTED;
+  a.q = q;
+  a.q_head_stride = q_head_stride;
   a.S = S;
   a.pos0 = pos0;
   a.group = n_q_heads / n_kv_heads;
