@@ -45,7 +45,7 @@ extern "C" {
 
 /* ---- element types ---------------------------------------------------- */
 typedef enum ie_dtype {
-  IE_DTYPE_F16 = 0,  /* the reference's storage type (kernels/*.cuh take half*)  */
+  IE_DTYPE_F16 = 0,  /* the reference's storage type (its kernel headers take half*) */
   IE_DTYPE_BF16 = 1  /* the BASELINE configs' storage type                        */
 } ie_dtype;
 
