@@ -25,6 +25,17 @@ def test_header_declares_expected_entry_points():
         assert n in names
 
 
+@pytest.mark.parametrize("compiler,std", [("gcc", "-std=c99"), ("g++", "-std=c++11")])
+def test_header_compiles_cleanly(tmp_path, compiler, std):
+    """The public header is plain C (and C++): no CUDA or torch types, and no
+    warnings under -Wall -Wextra for a caller that builds with -Werror."""
+    src = tmp_path / ("use.c" if compiler == "gcc" else "use.cpp")
+    src.write_text('#include "infengine_b200.h"\nint main(void) { return ie_version() ? 0 : 1; }\n')
+    r = subprocess.run([compiler, std, "-Wall", "-Wextra", "-Werror", "-pedantic", "-I", str(HEADER.parent), "-c",
+                        str(src), "-o", str(tmp_path / "use.o")], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+
+
 def test_library_exports_every_declared_symbol(ie):
     lib = ie.lib()
     for name in declared_functions():
