@@ -127,3 +127,36 @@ def test_attention_decode_bad_position(ie, cuda):
     assert np.all(got[1] == 0)
     _check_close(got[0:1], oracle.attention(q[:, 0:1], k[0], v[0], 100, dt), dt)
     assert ie.device_status() == 0  # cleared by the read above
+
+
+def test_prefill_attention_mma_kernel_selectable(tmp_path):
+    """IE_PREFILL_ATTN=mma runs prefill attention on the mma.sync kernel (kept
+    for A/B measurements); it meets the same bound against the oracle. Run in a
+    child process because the switch is read once per process."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    dt, S, pos0, nq, nkv = "bf16", 300, 100, 8, 2
+    rng = np.random.default_rng(77)
+    q = oracle.round_dt(rng.standard_normal((nq, S, 128), dtype=np.float32), dt)
+    k = oracle.round_dt(rng.standard_normal((nkv, pos0 + S, 128), dtype=np.float32), dt)
+    v = oracle.round_dt(rng.standard_normal((nkv, pos0 + S, 128), dtype=np.float32), dt)
+    np.savez(tmp_path / "in.npz", q=q, k=k, v=v)
+    root = Path(__file__).resolve().parent.parent
+    code = f"""
+import sys, numpy as np, torch
+sys.path.insert(0, {str(root)!r})
+import infengine_b200 as ie
+d = np.load({str(tmp_path / 'in.npz')!r})
+t = lambda a: torch.from_numpy(a).cuda().to(torch.bfloat16)
+out = torch.empty({S}, {nq * 128}, dtype=torch.bfloat16, device="cuda")
+ie.attention(t(d["q"]), t(d["k"]), t(d["v"]), out, {pos0}, n_kv_heads={nkv})
+torch.cuda.synchronize()
+assert ie.device_status() == 0
+np.save({str(tmp_path / 'out.npy')!r}, out.float().cpu().numpy())
+"""
+    env = dict(os.environ, IE_PREFILL_ATTN="mma")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    _check_close(np.load(tmp_path / "out.npy"), oracle.attention(q, k, v, pos0, dt), dt)
