@@ -205,11 +205,9 @@ class OursStep:
         self.ap = torch.empty(S, H, device=dev, dtype=torch.bfloat16)
         self.hp = torch.empty(S, F, device=dev, dtype=torch.bfloat16)
         self.op = torch.empty(S, H, device=dev, dtype=torch.bfloat16)
-        # stream-K workspace of the O / down projections (as the engine uses)
-        self.gws = torch.zeros(self.ie.gemm_workspace_size(), dtype=torch.uint8, device=dev)
 
     def release_prefill(self):
-        self.xp = self.qp = self.ap = self.hp = self.op = self.gws = None
+        self.xp = self.qp = self.ap = self.hp = self.op = None
 
     def prefill(self):
         """32 x [fused QKV+RoPE, O, gate/up+SwiGLU, down] at M = S tokens (positions 0..S-1)."""
@@ -217,9 +215,9 @@ class OursStep:
         for l, w in enumerate(self.layers):
             ie.qkv(self.xp, w["wq"], w["wk"], w["wv"], self.qp, self.kc[l], self.vc[l], CTX * HD, 0, self.cos,
                    self.sin)
-            ie.gemm(self.qp.view(S, H), w["wo"], self.ap, workspace=self.gws)  # stand-in for the attention output
+            ie.gemm(self.qp.view(S, H), w["wo"], self.ap)  # stand-in for the attention output
             ie.ffn_gate_up(self.xp, w["wg"], w["wu"], self.hp)
-            ie.gemm(self.hp, w["wd"], self.op, workspace=self.gws)
+            ie.gemm(self.hp, w["wd"], self.op)
 
     def prefill_flops(self):
         return 2.0 * self.S * L * LAYER_WEIGHT_ELEMS
@@ -400,16 +398,10 @@ def per_config(torch, step, stream, hbm_peak, tf_peak):
     for name, fn, flops in (
         ("qkv_6144x4096", lambda: [ie.qkv(step.xp, w["wq"], w["wk"], w["wv"], step.qp, step.kc[l], step.vc[l], CTX * HD,
                                           0, step.cos, step.sin) for l, w in enumerate(Ls)], 2 * S * 6144 * H),
-        ("o_4096x4096", lambda: [ie.gemm(step.qp.view(S, H), w["wo"], step.ap, workspace=step.gws) for w in Ls],
-         2 * S * H * H),
+        ("o_4096x4096", lambda: [ie.gemm(step.qp.view(S, H), w["wo"], step.ap) for w in Ls], 2 * S * H * H),
         ("gate_up_2x14336x4096", lambda: [ie.ffn_gate_up(step.xp, w["wg"], w["wu"], step.hp) for w in Ls],
          2 * S * 2 * F * H),
-        ("down_4096x14336", lambda: [ie.gemm(step.hp, w["wd"], step.op, workspace=step.gws) for w in Ls],
-         2 * S * H * F),
-        # the same two shapes without the stream-K workspace (whole tiles per CTA)
-        ("o_4096x4096_whole_tiles", lambda: [ie.gemm(step.qp.view(S, H), w["wo"], step.ap) for w in Ls],
-         2 * S * H * H),
-        ("down_4096x14336_whole_tiles", lambda: [ie.gemm(step.hp, w["wd"], step.op) for w in Ls], 2 * S * H * F),
+        ("down_4096x14336", lambda: [ie.gemm(step.hp, w["wd"], step.op) for w in Ls], 2 * S * H * F),
     ):
         t = timed(fn, reps=2) / L
         c3[name] = {"us": round(t * 1e6, 1), "tflops": round(flops / t / 1e12, 1),

@@ -87,30 +87,6 @@ int ie_gemm_add(ie_dtype dt, int M, int N, int K,
                 void* Y, int64_t ldy,
                 void* stream);
 
-/* ie_gemm / ie_gemm_add with a caller-owned workspace that lets the prefill
- * kernel (M > 16) split the k-loop of its tiles across all SMs when whole
- * tiles would leave the last wave partly empty (e.g. N = 4096 at M = 2048:
- * 256 tiles on 148 SMs). The workspace holds ie_gemm_workspace_size() bytes,
- * 16-byte aligned, zero-filled once when allocated; every call leaves it
- * ready for the next (its flag words lowered again; the partial sums it
- * holds need no clearing). Calls that share a workspace must not overlap on the GPU
- * (one stream, or ordered streams). Results are deterministic; their last
- * bits may differ from the unsplit call's (another fp32 summation order).
- * workspace == NULL runs the unsplit kernel. */
-size_t ie_gemm_workspace_size(void);
-int ie_gemm_ws(ie_dtype dt, int M, int N, int K,
-               const void* X, int64_t ldx,
-               const void* W, int64_t ldw,
-               void* Y, int64_t ldy,
-               void* workspace, size_t workspace_bytes,
-               void* stream);
-int ie_gemm_add_ws(ie_dtype dt, int M, int N, int K,
-                   const void* X, int64_t ldx,
-                   const void* W, int64_t ldw,
-                   void* Y, int64_t ldy,
-                   void* workspace, size_t workspace_bytes,
-                   void* stream);
-
 /* Same projection with unrounded fp32 output Y[M,N] (row stride ldy floats,
  * 16-byte aligned): the partial sums of a row-split (tensor-parallel) O or
  * down projection, to be summed across ranks before the one rounding. */

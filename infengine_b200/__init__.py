@@ -60,7 +60,7 @@ EXPORTED_SYMBOLS = (
     "ie_engine_destroy", "ie_engine_prefill", "ie_engine_decode", "ie_engine_verify", "ie_engine_set_position",
     "ie_engine_position", "ie_engine_stream", "ie_engine_step", "ie_engine_create_tp", "ie_add_f32",
     "ie_st_open", "ie_st_close", "ie_st_count", "ie_st_name", "ie_st_info", "ie_llama_load", "ie_llama_model_desc",
-    "ie_llama_model_shard", "ie_llama_model_free", "ie_gemm_workspace_size", "ie_gemm_ws", "ie_gemm_add_ws",
+    "ie_llama_model_shard", "ie_llama_model_free",
 )
 
 
@@ -89,11 +89,6 @@ def lib() -> ctypes.CDLL:
         L.ie_gemm.argtypes = [i32, i32, i32, i32, vp, i64, vp, i64, vp, i64, vp]
         L.ie_gemm_add.argtypes = [i32, i32, i32, i32, vp, i64, vp, i64, vp, i64, vp]
         L.ie_gemm_add.restype = i32
-        L.ie_gemm_workspace_size.restype = sz
-        L.ie_gemm_workspace_size.argtypes = []
-        for f in (L.ie_gemm_ws, L.ie_gemm_add_ws):
-            f.argtypes = [i32, i32, i32, i32, vp, i64, vp, i64, vp, i64, vp, sz, vp]
-            f.restype = i32
         L.ie_swiglu.argtypes = [i32, i32, i32, vp, vp, vp, vp]
         L.ie_ffn_workspace_size.restype = sz
         L.ie_ffn_workspace_size.argtypes = [i32, i32]
@@ -158,40 +153,24 @@ def _check(status: int, what: str) -> None:
 
 
 # -------------------------------------------------------------- C-ABI mirror
-def gemm_add(x, w, y, stream=None, workspace=None):
+def gemm_add(x, w, y, stream=None):
     """y[M,N] = round(y + round(x[M,K] . w[N,K]^T)) in place (ie_gemm_add):
-    a projection with the residual add fused. workspace: a zero-filled uint8
-    device tensor of gemm_workspace_size() bytes (ie_gemm_add_ws)."""
+    a projection with the residual add fused."""
     M, K = x.shape
     N = w.shape[0]
-    if workspace is None:
-        _check(lib().ie_gemm_add(_dt(x), M, N, K, _ptr(x), x.stride(0), _ptr(w), w.stride(0), _ptr(y), y.stride(0),
-                                 _stream(stream)), "ie_gemm_add")
-    else:
-        _check(lib().ie_gemm_add_ws(_dt(x), M, N, K, _ptr(x), x.stride(0), _ptr(w), w.stride(0), _ptr(y),
-                                    y.stride(0), _ptr(workspace), workspace.numel() * workspace.element_size(),
-                                    _stream(stream)), "ie_gemm_add_ws")
+    _check(lib().ie_gemm_add(_dt(x), M, N, K, _ptr(x), x.stride(0), _ptr(w), w.stride(0), _ptr(y), y.stride(0),
+                             _stream(stream)), "ie_gemm_add")
 
 
-def gemm_workspace_size() -> int:
-    """Bytes of the workspace ie_gemm_ws / ie_gemm_add_ws take on this device."""
-    return int(lib().ie_gemm_workspace_size())
-
-
-def gemm(x, w, y, M=None, N=None, K=None, ldx=None, ldw=None, ldy=None, stream=None, workspace=None):
-    """y[M,N] = x[M,K] . w[N,K]^T (ie_gemm; ie_gemm_ws with a workspace, see
-    gemm_add)."""
+def gemm(x, w, y, M=None, N=None, K=None, ldx=None, ldw=None, ldy=None, stream=None):
+    """y[M,N] = x[M,K] . w[N,K]^T (ie_gemm)."""
     M = x.shape[0] if M is None else M
     K = x.shape[-1] if K is None else K
     N = w.shape[0] if N is None else N
     ldx = x.stride(0) if ldx is None else ldx
     ldw = w.stride(0) if ldw is None else ldw
     ldy = y.stride(0) if ldy is None else ldy
-    if workspace is None:
-        _check(lib().ie_gemm(_dt(x), M, N, K, _ptr(x), ldx, _ptr(w), ldw, _ptr(y), ldy, _stream(stream)), "ie_gemm")
-    else:
-        _check(lib().ie_gemm_ws(_dt(x), M, N, K, _ptr(x), ldx, _ptr(w), ldw, _ptr(y), ldy, _ptr(workspace),
-                                workspace.numel() * workspace.element_size(), _stream(stream)), "ie_gemm_ws")
+    _check(lib().ie_gemm(_dt(x), M, N, K, _ptr(x), ldx, _ptr(w), ldw, _ptr(y), ldy, _stream(stream)), "ie_gemm")
 
 
 def ffn_fused(x, w_up, w_down, w_gate, out, workspace, stream=None):

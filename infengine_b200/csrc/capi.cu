@@ -65,7 +65,7 @@ int ie_device_status(int clear) {
 }
 
 static int gemm_store(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw,
-                      void* Y, int64_t ldy, bool residual, void* ws, size_t ws_bytes, void* stream) {
+                      void* Y, int64_t ldy, bool residual, void* stream) {
   if (!valid_dtype(dt) || M < 0 || N < 0 || K <= 0) return IE_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return IE_OK;
   if (K % 8) return IE_ERR_ALIGNMENT;
@@ -84,44 +84,17 @@ static int gemm_store(ie_dtype dt, int M, int N, int K, const void* X, int64_t l
   q.A = X; q.lda = ldx; q.B = W; q.ldb = ldw; q.M = M; q.N = N; q.K = K;
   q.D = Y; q.ldd = ldy; q.epi = TC_EPI_STORE;
   q.residual = residual;
-  if (ws) {
-    q.sk_ws = static_cast<float*>(ws);
-    q.sk_flags = reinterpret_cast<unsigned int*>(static_cast<char*>(ws) + tc_gemm_slot_bytes());
-  }
   return launch_tc_gemm(dt, q, as_stream(stream));
-}
-
-static int check_ws(void* ws, size_t ws_bytes) {
-  if (!ws) return ws_bytes == 0 ? IE_OK : IE_ERR_INVALID_ARG;
-  if (!aligned16(ws)) return IE_ERR_ALIGNMENT;
-  if (ws_bytes < tc_gemm_workspace_bytes()) return IE_ERR_WORKSPACE;
-  return IE_OK;
 }
 
 int ie_gemm(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, void* Y,
             int64_t ldy, void* stream) {
-  return gemm_store(dt, M, N, K, X, ldx, W, ldw, Y, ldy, false, nullptr, 0, stream);
+  return gemm_store(dt, M, N, K, X, ldx, W, ldw, Y, ldy, false, stream);
 }
 
 int ie_gemm_add(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, void* Y,
                 int64_t ldy, void* stream) {
-  return gemm_store(dt, M, N, K, X, ldx, W, ldw, Y, ldy, true, nullptr, 0, stream);
-}
-
-size_t ie_gemm_workspace_size(void) { return tc_gemm_workspace_bytes(); }
-
-int ie_gemm_ws(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, void* Y,
-               int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
-  const int s = check_ws(workspace, workspace_bytes);
-  if (s) return s;
-  return gemm_store(dt, M, N, K, X, ldx, W, ldw, Y, ldy, false, workspace, workspace_bytes, stream);
-}
-
-int ie_gemm_add_ws(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, void* Y,
-                   int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
-  const int s = check_ws(workspace, workspace_bytes);
-  if (s) return s;
-  return gemm_store(dt, M, N, K, X, ldx, W, ldw, Y, ldy, true, workspace, workspace_bytes, stream);
+  return gemm_store(dt, M, N, K, X, ldx, W, ldw, Y, ldy, true, stream);
 }
 
 int ie_gemm_f32out(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, float* Y,

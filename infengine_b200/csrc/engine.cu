@@ -55,8 +55,6 @@ struct Engine {
       *ids = nullptr;
   void* lm_ws = nullptr;
   size_t lm_ws_bytes = 0;
-  void* gemm_ws = nullptr;  // stream-K workspace of the prefill O / down projections
-  size_t gemm_ws_bytes = 0;
   std::vector<int> pos_host;
   long long step_host = 0;
   cudaGraph_t graph = nullptr;
@@ -94,7 +92,7 @@ int check(cudaError_t e) { return e == cudaSuccess ? IE_OK : IE_ERR_LAUNCH; }
 // NVLink exchange kernel (decode rows) or NCCL (longer chunks).
 int proj_add(Engine& E, int M, int K, const void* X, const void* W) {
   const int H = E.d.hidden;
-  if (E.world == 1) return ie_gemm_add_ws(E.dt, M, H, K, X, K, W, K, E.x, H, E.gemm_ws, E.gemm_ws_bytes, E.st);
+  if (E.world == 1) return ie_gemm_add(E.dt, M, H, K, X, K, W, K, E.x, H, E.st);
   if (E.has_ex && M <= 16 && M <= E.ex.max_rows)
     return ie_gemm_allreduce_add(E.dt, M, H, K, X, K, W, K, E.x, H, &E.ex, E.st);
   IE_TRY(ie_gemm_f32out(E.dt, M, H, K, X, K, W, K, E.part, H, E.st));
@@ -180,7 +178,7 @@ void release(Engine* E) {
   if (E->exec) cudaGraphExecDestroy(E->exec);
   if (E->graph) cudaGraphDestroy(E->graph);
   void* bufs[] = {E->x,       E->a,     E->q,    E->attn,  E->h,     E->kv,    E->tok_in, E->positions,
-                  E->history, E->step,  E->chunk, E->ids,  E->lm_ws, E->part, E->keys,   E->gemm_ws};
+                  E->history, E->step,  E->chunk, E->ids,  E->lm_ws, E->part, E->keys};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (E->own_stream && E->st) cudaStreamDestroy(E->st);
@@ -274,10 +272,6 @@ int ie_engine_create_tp(ie_dtype dt, const ie_llama_desc* desc, int max_batch, i
   alloc(reinterpret_cast<void**>(&E->chunk), R * sizeof(int));
   alloc(reinterpret_cast<void**>(&E->ids), R * sizeof(int));
   alloc(&E->lm_ws, E->lm_ws_bytes);
-  if (E->world == 1 && max_prefill > 16) {
-    E->gemm_ws_bytes = ie_gemm_workspace_size();
-    alloc(&E->gemm_ws, E->gemm_ws_bytes);
-  }
   if (E->world > 1) {
     alloc(reinterpret_cast<void**>(&E->part), R * H * sizeof(float));
     alloc(reinterpret_cast<void**>(&E->keys), (size_t)(max_batch > 16 ? max_batch : 16) * sizeof(unsigned long long));
@@ -288,7 +282,6 @@ int ie_engine_create_tp(ie_dtype dt, const ie_llama_desc* desc, int max_batch, i
          cudaMemsetAsync(E->positions, 0, max_batch * sizeof(int), E->st) == cudaSuccess &&
          cudaMemsetAsync(E->step, 0, sizeof(int), E->st) == cudaSuccess &&
          cudaMemsetAsync(E->lm_ws, 0, E->lm_ws_bytes, E->st) == cudaSuccess &&
-         (!E->gemm_ws || cudaMemsetAsync(E->gemm_ws, 0, E->gemm_ws_bytes, E->st) == cudaSuccess) &&
          cudaStreamSynchronize(E->st) == cudaSuccess;
   }
   if (!ok) {

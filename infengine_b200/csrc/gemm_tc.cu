@@ -25,22 +25,6 @@
 //   ARGMAX — 256 consecutive vocabulary rows.
 // No TMA multicast and no clusters: every load reads this GPU's own memory.
 //
-// Work split. By default CTA c takes tiles c, c + grid, ... (data-parallel).
-// With a caller-owned workspace and a plain-store epilogue whose tile count
-// leaves the last wave partly empty (O and down at M = 2048: 256 tiles on 148
-// SMs, 1.73 waves), the (tile, k-block) iterations are split evenly instead
-// (stream-K): CTA c takes iterations [c*I/G, (c+1)*I/G) of I = tiles x
-// k-blocks in tile order, as segments (tile, k-blocks [k0, k1)). A segment
-// that does not start at k-block 0 can only be a CTA's first one; its fp32
-// accumulator goes to that CTA's workspace slot and a flag is raised. The
-// CTA that holds a tile's k-block 0 (its last segment, if the tile goes on
-// past its range) waits for the flags of the CTAs after it that hold the
-// rest of the tile, adds their partial sums in k order (deterministic) and
-// runs the epilogue; it then lowers the flags, leaving the workspace as it
-// found it. A CTA only ever waits for first segments of later CTAs, which
-// wait for nothing, so the waits cannot form a cycle; they are bounded like
-// every other wait.
-//
 // Every mbarrier wait is bounded by the global timer; a wait that gives up
 // records IE_ERR_TIMEOUT in a device status word (ie_device_status()), makes
 // every role leave its loop, drains the copies and MMAs the CTA issued and
@@ -76,45 +60,7 @@ struct TcArgs {
   TcGemmParams p;
   int nm, nn, nk;
   int heads;  // QKV: n_q_heads + 2 * n_kv_heads
-  int sk;     // 1: stream-K split of the iterations (TC_EPI_STORE with a workspace)
 };
-
-// This CTA's work as segments (tile, k-blocks [k0, k1)).
-struct Segs {
-  long long it, end, step;
-  int nk;
-  bool sk;
-};
-__device__ __forceinline__ long long sk_begin(long long total, int c) { return total * c / gridDim.x; }
-__device__ __forceinline__ Segs segs_begin(bool sk, int num_tiles, int nk) {
-  Segs s;
-  s.nk = nk;
-  s.sk = sk;
-  const long long total = (long long)num_tiles * nk;
-  if (sk) {
-    s.it = sk_begin(total, blockIdx.x);
-    s.end = sk_begin(total, blockIdx.x + 1);
-    s.step = 0;
-  } else {
-    s.it = (long long)blockIdx.x * nk;
-    s.end = total;
-    s.step = (long long)gridDim.x * nk;
-  }
-  return s;
-}
-__device__ __forceinline__ bool segs_next(Segs& s, int& tile, int& k0, int& k1) {
-  if (s.it >= s.end) return false;
-  tile = (int)(s.it / s.nk);
-  k0 = (int)(s.it - (long long)tile * s.nk);
-  if (s.sk) {
-    k1 = (int)min((long long)s.nk, (long long)k0 + (s.end - s.it));
-    s.it += k1 - k0;
-  } else {
-    k1 = s.nk;
-    s.it += s.step;
-  }
-  return true;
-}
 
 // ------------------------------------------------------------ PTX helpers
 using namespace tc;
@@ -124,22 +70,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 template <typename T>
 __device__ __forceinline__ uint32_t idesc_f16() {
   return tc::idesc_f16<T>(BM, BN);
-}
-// Bounded wait for another CTA's flag (acquire at GPU scope).
-__device__ __forceinline__ bool wait_flag(const unsigned int* f, volatile int* abort_flag) {
-  const unsigned long long t0 = globaltimer();
-  while (true) {
-    unsigned int v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-    if (v) return true;
-    if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitNs) {
-      atomicExch(&g_tc_status, IE_ERR_TIMEOUT);
-      *abort_flag = 1;
-      return false;
-    }
-    __nanosleep(64);
-  }
 }
 
 // Store 32 consecutive values of one output row (columns col0.. col0+31,
@@ -204,7 +134,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TILE_BYTES);
   // bars: full[0..S), empty[S..2S), acc_full[2S..2S+2), acc_empty[2S+2..2S+4), drain[2S+4]
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 8);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   int* issued_p = reinterpret_cast<int*>(tmem_holder + 2);
   int* consumed_p = reinterpret_cast<int*>(tmem_holder + 3);
@@ -218,10 +148,6 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
   auto accf_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + a); };
   auto acce_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + 2 + a); };
   const uint32_t drain_bar = smem_u32(bars + 2 * STAGES + 4);
-  // stream-K hand-offs, each used at most once per CTA: partial written by
-  // the 4 epilogue warps; other CTAs' partials ready; partials read
-  const uint32_t sk_pub = smem_u32(bars + 2 * STAGES + 5), sk_ready = smem_u32(bars + 2 * STAGES + 6),
-                 sk_read = smem_u32(bars + 2 * STAGES + 7);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -233,9 +159,6 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
       mbar_init(acce_bar(a), 4);
     }
     mbar_init(drain_bar, 1);
-    mbar_init(sk_pub, 4);
-    mbar_init(sk_ready, 1);
-    mbar_init(sk_read, 4);
     *abort_flag = 0;
     *issued_p = 0;
     *consumed_p = 0;
@@ -263,11 +186,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
       // ------------------------------------------------ TMA producer
       int stage = 0, issued = 0;
       uint32_t phase = 0;
-      Segs sg = segs_begin(args.sk != 0, num_tiles, args.nk);
-      int tile, k0, k1;
-      while (!*abort_flag && segs_next(sg, tile, k0, k1)) {
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
         const int mb = tile % args.nm, nb = tile / args.nm;
-        for (int kb = k0; kb < k1; ++kb) {
+        for (int kb = 0; kb < args.nk; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag)) break;
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
           mbar_expect_tx(full_bar(stage), STAGE_BYTES);
@@ -292,21 +213,19 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
       int stage = 0, consumed = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool issued_any = false;
-      Segs sg = segs_begin(args.sk != 0, num_tiles, args.nk);
-      int tile, k0, k1;
-      while (!*abort_flag && segs_next(sg, tile, k0, k1)) {
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
         if (!mbar_wait(acce_bar(acc), acc_phase ^ 1, abort_flag)) break;
         fence_after();
         const uint32_t d_tmem = tmem + acc * BN;
         bool ok = true;
-        for (int kb = k0; kb < k1; ++kb) {
+        for (int kb = 0; kb < args.nk; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
           fence_after();
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
           const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + A_TILE);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            mma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb != k0 || k != 0) ? 1u : 0u);
+            mma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
           mma_commit(empty_bar(stage));
           issued_any = true;
           ++consumed;
@@ -332,12 +251,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
     const int row = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    Segs sg = segs_begin(args.sk != 0, num_tiles, args.nk);
-    int tile, k0, k1;
-    const long long sk_total = (long long)num_tiles * args.nk;
-    while (!*abort_flag && segs_next(sg, tile, k0, k1)) {
+    for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
       const int mb = tile % args.nm, nb = tile / args.nm;
-      bool publish = false;
       if (!mbar_wait(accf_bar(acc), acc_phase, abort_flag)) break;
       fence_after();
       const uint32_t tbase = tmem + acc * BN + ((uint32_t)(quad * 32) << 16);
@@ -352,59 +267,11 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
           if (mvalid) store_row32_f32(drow, nb * BN + c * 32, p.N, v);
         }
       } else if constexpr (EPI == TC_EPI_STORE) {
-        if (args.sk && k0 > 0) {
-          // part of a tile that another CTA finishes: fp32 partial sums to
-          // this CTA's workspace slot (row-major 128 x 256)
-          float* slot = p.sk_ws + (size_t)blockIdx.x * (BM * BN) + (size_t)row * BN;
+        T* drow = static_cast<T*>(p.D) + (int64_t)m * p.ldd;
 #pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            tmem_ld32(tbase + c * 32, v);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              __stcg(reinterpret_cast<float4*>(slot + c * 32) + j,
-                     make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
-          }
-          __threadfence();
-          publish = true;
-        } else {
-          // k-blocks [0, k1) here; with stream-K the rest of the tile comes
-          // from the CTAs [blockIdx.x + 1, c_last], added in k order
-          int c_last = blockIdx.x;
-          if (args.sk && k1 < args.nk) {
-            const long long tile_end = (long long)(tile + 1) * args.nk;
-            while (c_last + 1 < (int)gridDim.x && sk_begin(sk_total, c_last + 1) < tile_end) ++c_last;
-            if (warp == 2 && lane == 0) {
-              bool fok = true;
-              for (int c = blockIdx.x + 1; c <= c_last && fok; ++c) fok = wait_flag(p.sk_flags + c, abort_flag);
-              mbar_arrive(sk_ready);
-            }
-            if (!mbar_wait(sk_ready, 0, abort_flag) || *abort_flag) break;
-          }
-          T* drow = static_cast<T*>(p.D) + (int64_t)m * p.ldd;
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            tmem_ld32(tbase + c * 32, v);
-            for (int cc = blockIdx.x + 1; cc <= c_last; ++cc) {
-              const float4* part = reinterpret_cast<const float4*>(p.sk_ws + (size_t)cc * (BM * BN) +
-                                                                   (size_t)row * BN + c * 32);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 q = __ldcg(part + j);
-                v[4 * j] += q.x;
-                v[4 * j + 1] += q.y;
-                v[4 * j + 2] += q.z;
-                v[4 * j + 3] += q.w;
-              }
-            }
-            if (mvalid) store_row32<T>(drow, nb * BN + c * 32, p.N, v, p.residual);
-          }
-          if (c_last > (int)blockIdx.x) {
-            // every epilogue warp has read the partials: lower their flags
-            __syncwarp();
-            if (lane == 0) mbar_arrive(sk_read);
-            if (warp == 2 && lane == 0 && mbar_wait(sk_read, 0, abort_flag))
-              for (int c = blockIdx.x + 1; c <= c_last; ++c) p.sk_flags[c] = 0u;
-          }
+        for (int c = 0; c < BN / 32; ++c) {
+          tmem_ld32(tbase + c * 32, v);
+          if (mvalid) store_row32<T>(drow, nb * BN + c * 32, p.N, v, p.residual);
         }
       } else if constexpr (EPI == TC_EPI_SWIGLU) {
         T* drow = static_cast<T*>(p.D) + (int64_t)m * p.ldd;
@@ -508,14 +375,6 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_bar(acc));
-      if (publish) {
-        // all four warps' partial rows are in the workspace: raise the flag
-        if (lane == 0) mbar_arrive(sk_pub);
-        if (warp == 2 && lane == 0 && mbar_wait(sk_pub, 0, abort_flag)) {
-          __threadfence();
-          asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p.sk_flags + blockIdx.x), "r"(1u) : "memory");
-        }
-      }
       if constexpr (EPI == TC_EPI_ARGMAX) {
         // each epilogue warp counts its own part of the tile after its
         // atomics; the warp that brings the count to 4 * tiles finalizes
@@ -592,7 +451,7 @@ int launch_t(TcArgs& a, cudaStream_t st) {
   }
   const int tiles = a.nm * a.nn;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.sk ? sm_count() : (tiles < sm_count() ? tiles : sm_count()));
+  cfg.gridDim = dim3(tiles < sm_count() ? tiles : sm_count());
   cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = st;
@@ -658,18 +517,7 @@ int launch_tc_gemm(ie_dtype dt, const TcGemmParams& p, cudaStream_t st) {
     default:
       return IE_ERR_UNSUPPORTED;
   }
-  // stream-K where the last wave of tiles would leave SMs idle
-  {
-    const int P = sm_count(), tiles = a.nm * a.nn;
-    a.sk = (p.sk_ws && p.sk_flags && p.epi == TC_EPI_STORE && tiles % P != 0 && tiles >= P && tiles < 4 * P) ? 1 : 0;
-  }
   return dt == IE_DTYPE_BF16 ? dispatch<__nv_bfloat16>(a, p.epi, st) : dispatch<__half>(a, p.epi, st);
-}
-
-size_t tc_gemm_slot_bytes() { return (size_t)sm_count() * BM * BN * sizeof(float); }
-
-size_t tc_gemm_workspace_bytes() {
-  return tc_gemm_slot_bytes() + ((size_t)sm_count() * sizeof(unsigned int) + 255) / 256 * 256;
 }
 
 int read_tc_status(bool clear) {

@@ -48,19 +48,10 @@ struct TcGemmParams {
   const int* positions = nullptr;
   int64_t cache_batch_stride = 0;
   int cache_rows = 0;
-  // TC_EPI_STORE: caller-owned, zero-initialised stream-K workspace (fp32
-  // partial tiles, one slot per CTA, then one flag per CTA); null = no split
-  float* sk_ws = nullptr;
-  unsigned int* sk_flags = nullptr;
 };
 
 // Returns an IE_* status.
 int launch_tc_gemm(ie_dtype dt, const TcGemmParams& p, cudaStream_t st);
-
-// Bytes of the stream-K workspace on the current device: one fp32 partial
-// tile per SM (tc_gemm_slot_bytes()), then one flag per SM.
-size_t tc_gemm_workspace_bytes();
-size_t tc_gemm_slot_bytes();
 
 // Device status word written by timed-out waits (IE_OK or IE_ERR_TIMEOUT).
 int read_tc_status(bool clear);

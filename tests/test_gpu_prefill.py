@@ -134,54 +134,3 @@ def test_lm_head_argmax_tensor_core(ie, cuda, dt, M):
     idx2 = cuda.full((M,), -1, dtype=cuda.int32, device="cuda")
     ie.lm_head_argmax(x, w, ws, idx_out=idx2)
     assert np.array_equal(idx2.cpu().numpy(), got_idx)
-
-
-def _sk_workspace(ie, cuda):
-    return cuda.zeros(ie.gemm_workspace_size(), dtype=cuda.uint8, device="cuda")
-
-
-def _sk_flags(ie, cuda, ws):
-    sms = cuda.cuda.get_device_properties(0).multi_processor_count
-    flag_bytes = (sms * 4 + 255) // 256 * 256
-    return ws[ws.numel() - flag_bytes:]
-
-
-@pytest.mark.parametrize("dt", ["bf16", "f16"])
-@pytest.mark.parametrize("M,N,K", [
-    (2048, 4096, 4096),   # O projection: 256 tiles on 148 SMs
-    (2048, 4096, 14336),  # down projection
-    (2000, 4000, 1000),   # ragged M, N and K (k-blocks not a multiple of 64)
-    (1200, 5000, 520),    # 200 tiles, 9 k-blocks: several CTAs per tile
-])
-def test_gemm_stream_k(ie, cuda, dt, M, N, K):
-    """ie_gemm_ws: the k-loop split across all SMs (stream-K) meets the same
-    bound as the unsplit kernel, repeats bit for bit, and leaves the
-    workspace's flag words lowered."""
-    d = oracle.seeded_inputs(M + 3 * N + K, {"x": (M, K), "w": (N, K)}, dt)
-    x, w = to_dev(d["x"], dt), to_dev(d["w"], dt)
-    ws = _sk_workspace(ie, cuda)
-    y = cuda.full((M, N), float("nan"), dtype=torch_dtype(dt), device="cuda")
-    ie.gemm(x, w, y, workspace=ws)
-    got = from_dev(y)
-    assert not np.isnan(got).any()
-    assert_within_one_rounding(got, oracle.gemm_fp32(d["x"], d["w"]), dt)
-    assert int(_sk_flags(ie, cuda, ws).count_nonzero()) == 0
-    y2 = cuda.full((M, N), float("nan"), dtype=torch_dtype(dt), device="cuda")
-    ie.gemm(x, w, y2, workspace=ws)
-    assert cuda.equal(y, y2)
-
-
-def test_gemm_add_stream_k(ie, cuda):
-    """ie_gemm_add_ws (the engine's prefill O / down call): the residual add
-    fused after the split k-loop is exactly round(r + ie_gemm_ws(x, w))."""
-    dt, M, N, K = "bf16", 2048, 4096, 14336
-    d = oracle.seeded_inputs(91, {"x": (M, K), "w": (N, K), "r": (M, N)}, dt)
-    x, w = to_dev(d["x"], dt), to_dev(d["w"], dt)
-    ws = _sk_workspace(ie, cuda)
-    t = cuda.empty((M, N), dtype=torch_dtype(dt), device="cuda")
-    ie.gemm(x, w, t, workspace=ws)
-    y = to_dev(d["r"], dt)
-    ie.gemm_add(x, w, y, workspace=ws)
-    want = oracle.residual_add(d["r"], from_dev(t), dt)
-    assert np.array_equal(from_dev(y), want)
-    assert int(_sk_flags(ie, cuda, ws).count_nonzero()) == 0
