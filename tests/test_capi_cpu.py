@@ -105,6 +105,40 @@ def test_invalid_arguments_rejected_without_device(ie):
     assert lib.ie_argmax(0, 1, 100, fake, 50, fake, None) == -1
 
 
+def test_attention_rejects_bad_arguments_without_device(ie):
+    """ie_attention (prefill / chunk) and ie_attention_decode validate shapes,
+    strides and alignment before any launch."""
+    lib = ie.lib()
+    vp = ctypes.c_void_p
+    f = vp(0x1000)
+    chs = 2048 * 128  # cache head stride: 2048 positions
+    # ie_attention(dt, S, pos0, nq, nkv, head_dim, q, q_hs, k, v, chs, out, ld_out, stream)
+    ok = lambda **kw: dict(dict(dt=1, S=300, pos0=0, nq=32, nkv=8, hd=128, q=f, qhs=300 * 128, k=f, v=f, chs=chs,
+                                out=f, ldo=4096), **kw)
+    call = lambda a: lib.ie_attention(a["dt"], a["S"], a["pos0"], a["nq"], a["nkv"], a["hd"], a["q"], a["qhs"],
+                                      a["k"], a["v"], a["chs"], a["out"], a["ldo"], None)
+    assert call(ok(dt=5)) == -1                        # unknown dtype
+    assert call(ok(S=-1)) == -1                        # negative length
+    assert call(ok(hd=64)) == -3                       # head_dim other than 128
+    assert call(ok(nq=30)) == -3                       # query heads not a multiple of KV heads
+    assert call(ok(S=0)) == 0                          # empty chunk: no-op
+    assert call(ok(q=None)) == -1                      # null operand
+    assert call(ok(k=vp(0x1008))) == -2                # cache not 16-byte aligned
+    assert call(ok(ldo=4000)) == -1                    # output row shorter than the heads
+    assert call(ok(qhs=100 * 128)) == -1               # q head stride shorter than S rows
+    assert call(ok(pos0=1900)) == -1                   # chunk runs past the cache (1900 + 300 > 2048)
+    # ie_attention_decode(dt, R, rows_per_seq, nq, nkv, hd, q, q_hs, k, v, chs, cbs, cache_rows, positions,
+    #                     pos0, out, ld_out, stream)
+    dec = lambda R=1, rps=1, nq=32, nkv=8, rows=2048, pos0=0, k=f: lib.ie_attention_decode(
+        1, R, rps, nq, nkv, 128, f, 128 * max(R, 1), k, f, chs, 0, rows, None, pos0, f, 4096, None)
+    assert dec(nq=24) == -3                            # group of 3 query heads per KV head
+    assert dec(R=3, rps=2) == -1                       # rows not a whole number of sequences
+    assert dec(rows=4096) == -1                        # cache rows beyond the head stride
+    assert dec(pos0=2048) == -1                        # position outside the cache
+    assert dec(k=vp(0x1004)) == -2                     # cache not 16-byte aligned
+    assert dec(R=0) == 0                               # no rows: no-op
+
+
 def test_workspace_sizes(ie):
     assert ie.ffn_workspace_bytes(1, 14336) >= 14336 * 2
     assert ie.ffn_workspace_size(5) == 2 * 5 * 14336 * 2  # reference ffn.cu:35-37
