@@ -139,6 +139,32 @@ def test_attention_rejects_bad_arguments_without_device(ie):
     assert dec(R=0) == 0                               # no rows: no-op
 
 
+def test_norm_embed_add_reject_bad_arguments_without_device(ie):
+    """ie_rmsnorm, ie_embed and ie_add_f32 validate before any launch."""
+    from infengine_b200.engine import _bind
+    _bind()
+    lib = ie.lib()
+    vp = ctypes.c_void_p
+    f = vp(0x1000)
+    rms = lambda dt=1, M=1, H=4096, x=f, ldx=4096, w=f, out=f, ldo=4096: lib.ie_rmsnorm(dt, M, H, x, ldx, w, out, ldo,
+                                                                                     1e-5, None)
+    assert rms(dt=9) == -1                 # unknown dtype
+    assert rms(M=0) == 0                   # no rows: no-op
+    assert rms(w=None) == -1               # null weight
+    assert rms(ldx=4000) == -1             # row stride shorter than the row
+    assert rms(H=4092, ldx=4096) == -2     # row not a whole number of 16-byte chunks
+    assert rms(x=vp(0x1004)) == -2         # misaligned input
+    assert rms(H=20480, ldx=20480, ldo=20480) == -3  # wider than one CTA's 16-byte chunks
+    emb = lambda M=1, H=4096, V=128256, tok=f, ldo=4096: lib.ie_embed(1, M, H, V, tok, f, f, ldo, None)
+    assert emb(V=0) == -1                  # empty vocabulary
+    assert emb(M=0) == 0                   # no tokens: no-op
+    assert emb(tok=None) == -1             # null token array
+    assert emb(H=4100, ldo=4104) == -2     # row not a whole number of 16-byte chunks
+    lib.ie_add_f32.argtypes = [ctypes.c_int, vp, vp, ctypes.c_size_t, vp]
+    assert lib.ie_add_f32(1, None, f, 16, None) == -1   # null input
+    assert lib.ie_add_f32(1, None, None, 0, None) == 0  # empty: no-op
+
+
 def test_workspace_sizes(ie):
     assert ie.ffn_workspace_bytes(1, 14336) >= 14336 * 2
     assert ie.ffn_workspace_size(5) == 2 * 5 * 14336 * 2  # reference ffn.cu:35-37
