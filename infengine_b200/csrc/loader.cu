@@ -1,4 +1,4 @@
-// Safetensors weight loader (SURVEY f3; the reference's
+// Safetensors weight loader (the reference's
 // ModelWeights::from_safetensors, kernels/model_weights.cu:80-154).
 //
 // The reference parses the header with nlohmann/json, makes one cudaMalloc

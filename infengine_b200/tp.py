@@ -1,7 +1,7 @@
 """Megatron-style tensor parallelism of the weight-matmul hot path.
 
 The reference runs on one GPU; this splits its projections across the GPUs of
-one box:
+one machine:
 
 * Q/K/V column-split by heads: rank r owns query heads
   [r*NQ/t, (r+1)*NQ/t) and KV heads [r*NKV/t, (r+1)*NKV/t) (ie_qkv on the
