@@ -868,7 +868,7 @@ def run_ours(torch, dist, dev, args, world, rank, local, hbm_peak, tf_peak, tf_p
         result["prefill"] = {"workload": f"M=2048 tokens, tp{world}: 32 x [QKV+RoPE, O+allreduce, gate/up+SwiGLU, "
                                          f"down+allreduce] + lm_head(last row)", "ms": round(pre_s * 1e3, 3),
                              "tflops_aggregate": round(tflops, 1),
-                             "frac_of_n_x_sustained": round(tflops / (world * tf_peak_sus), 4)}
+                             "frac_of_n_x_burst": round(tflops / (world * tf_peak), 4)}
         gp.reset()
         del gp
     else:
@@ -892,11 +892,14 @@ def run_ours(torch, dist, dev, args, world, rank, local, hbm_peak, tf_peak, tf_p
                     gp.replay()
             pre_s = timed(torch, stream, pre, world, dev) / 1e3 / reps
         tflops = step.prefill_flops() / pre_s / 1e12
+        # the timed region is a few chains of ~25 ms, not a seconds-long loop:
+        # the burst peak is the denominator (the sustained figure is shown too)
         result["prefill"] = {
             "workload": "M=2048 tokens: 32 x [fused QKV+RoPE 6144x4096, O 4096x4096, gate/up+SwiGLU 2x14336x4096, "
                         "down 4096x14336]", "ms": round(pre_s * 1e3, 3), "tflops": round(tflops, 1),
-            "peak_tflops": tf_peak_sus, "frac": round(tflops / tf_peak_sus, 4),
-            "peak_source": f"{peak_src} bf16 sustained (a {pre_s * 1e3:.0f} ms chain)",
+            "peak_tflops": tf_peak, "frac": round(tflops / tf_peak, 4),
+            "peak_source": f"{peak_src} bf16 burst ({reps} chains of {pre_s * 1e3:.0f} ms)",
+            "frac_of_sustained": round(tflops / tf_peak_sus, 4),
             "gpu_launches": 4 * L,
         }
         del gp

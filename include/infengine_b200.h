@@ -173,8 +173,13 @@ int ie_qkv_batched(ie_dtype dt, int B, int H, int n_q_heads, int n_kv_heads, int
  *   caches [n_kv_heads][.][128] (head stride cache_head_stride);
  *   out    [S][n_q_heads*128] (row stride ld_out), the input of the O projection.
  * Scores are rounded to dt, scaled by rsqrt(128) and rounded, softmaxed with
- * the reference's roundings; head_dim 128, n_q_heads / n_kv_heads <= 8,
- * (pos0 + S) * group <= ~50k (scores of a row are kept on chip). */
+ * the reference's roundings. Limits: head_dim 128; n_q_heads a multiple of
+ * n_kv_heads; pos0 + S <= INT_MAX and within cache_head_stride / 128 rows.
+ * S <= 16 runs the decode kernel below, so its limits apply (group
+ * n_q_heads / n_kv_heads in {1, 2, 4, 8}, (pos0 + S) * group <= ~270k).
+ * Longer chunks run the tensor-core kernel, which streams scores and needs
+ * only ceil(S / 128) <= 65535 and n_q_heads <= 65535. A limit that is not met
+ * returns IE_ERR_UNSUPPORTED (or IE_ERR_INVALID_ARG for a too-small cache). */
 int ie_attention(ie_dtype dt, int S, int pos0, int n_q_heads, int n_kv_heads, int head_dim,
                  const void* q, int64_t q_head_stride,
                  const void* k_cache, const void* v_cache, int64_t cache_head_stride,
@@ -213,7 +218,10 @@ int ie_attention_decode(ie_dtype dt, int R, int rows_per_seq, int n_q_heads, int
  * key_out [M] packed 64-bit keys; the max of keys across vocab shards is the
  * key of the global winner (ie_argmax_key_index() recovers the id).
  * workspace: ie_lm_head_argmax_workspace_size(M) bytes, zeroed once by the
- * caller when allocated; every call leaves it zeroed again.
+ * caller when allocated; every call that completes leaves it zeroed again.
+ * A call whose device-side wait timed out (IE_ERR_TIMEOUT in
+ * ie_device_status) may leave keys and the completion counter set: the
+ * caller must zero the workspace again before its next use.
  */
 size_t ie_lm_head_argmax_workspace_size(int M);
 int ie_lm_head_argmax(ie_dtype dt, int M, int K, int V, int64_t vocab_offset,

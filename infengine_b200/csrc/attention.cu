@@ -514,7 +514,7 @@ extern "C" int ie_attention_decode(ie_dtype dt, int R, int rows_per_seq, int n_q
   if (ld_out < (int64_t)n_q_heads * 128 || q_head_stride < (int64_t)R * 128) return IE_ERR_INVALID_ARG;
   if (cache_head_stride < (int64_t)cache_rows * 128) return IE_ERR_INVALID_ARG;
   if (R / rows_per_seq > 1 && cache_batch_stride < (int64_t)n_kv_heads * cache_head_stride) return IE_ERR_INVALID_ARG;
-  if (!positions && pos0 + R > cache_rows) return IE_ERR_INVALID_ARG;
+  if (!positions && (int64_t)pos0 + R > cache_rows) return IE_ERR_INVALID_ARG;
   FdParams p;
   p.q = q;
   p.q_head_stride = q_head_stride;
@@ -825,7 +825,8 @@ extern "C" int ie_attention(ie_dtype dt, int S, int pos0, int n_q_heads, int n_k
       (q_head_stride % 8) || (ld_out % 8))
     return IE_ERR_ALIGNMENT;
   if (ld_out < (int64_t)n_q_heads * 128 || q_head_stride < (int64_t)S * 128) return IE_ERR_INVALID_ARG;
-  if (cache_head_stride < (int64_t)(pos0 + S) * 128) return IE_ERR_INVALID_ARG;
+  if ((int64_t)pos0 + S > INT_MAX) return IE_ERR_INVALID_ARG;
+  if (cache_head_stride < ((int64_t)pos0 + S) * 128) return IE_ERR_INVALID_ARG;
   if (S <= 16)  // few rows: the split-KV kernel (exact chain)
     return ie_attention_decode(dt, S, S, n_q_heads, n_kv_heads, head_dim, q, q_head_stride, k_cache, v_cache,
                                cache_head_stride, 0, pos0 + S, nullptr, pos0, out, ld_out, stream);

@@ -310,7 +310,7 @@ int ie_engine_prefill(ie_engine* eng, int seq, const int* tokens, int n, int* ne
   Engine& E = *eng->e;
   if (seq < 0 || seq >= E.B) return IE_ERR_INVALID_ARG;
   const int pos0 = E.pos_host[seq];
-  if (n > E.max_rows || pos0 + n > E.ctx) return IE_ERR_UNSUPPORTED;
+  if (n > E.max_rows || (int64_t)pos0 + n > E.ctx) return IE_ERR_UNSUPPORTED;
   for (int i = 0; i < n; ++i)
     if (tokens[i] < 0 || tokens[i] >= E.d.vocab) return IE_ERR_INVALID_ARG;
   IE_TRY(check(cudaMemcpyAsync(E.chunk, tokens, n * sizeof(int), cudaMemcpyHostToDevice, E.st)));
@@ -331,7 +331,7 @@ int ie_engine_decode(ie_engine* eng, int n_steps, int* out_tokens) {
   Engine& E = *eng->e;
   if (n_steps == 0) return IE_OK;
   for (int b = 0; b < E.B; ++b)
-    if (E.pos_host[b] + n_steps > E.ctx) return IE_ERR_UNSUPPORTED;
+    if ((int64_t)E.pos_host[b] + n_steps > E.ctx) return IE_ERR_UNSUPPORTED;
   IE_TRY(capture(E));
   int done = 0;
   while (done < n_steps) {
@@ -355,7 +355,7 @@ int ie_engine_verify(ie_engine* eng, int seq, const int* tokens, int M, int* out
   Engine& E = *eng->e;
   if (seq < 0 || seq >= E.B || M > 16 || M > E.max_rows) return IE_ERR_INVALID_ARG;
   const int pos0 = E.pos_host[seq];
-  if (pos0 + M > E.ctx) return IE_ERR_UNSUPPORTED;
+  if ((int64_t)pos0 + M > E.ctx) return IE_ERR_UNSUPPORTED;
   for (int i = 0; i < M; ++i)
     if (tokens[i] < 0 || tokens[i] >= E.d.vocab) return IE_ERR_INVALID_ARG;
   IE_TRY(check(cudaMemcpyAsync(E.chunk, tokens, M * sizeof(int), cudaMemcpyHostToDevice, E.st)));

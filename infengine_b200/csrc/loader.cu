@@ -22,6 +22,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 #include <cmath>
+#include <cstdint>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -209,8 +210,12 @@ int parse_header(ie_safetensors& f, const char* hdr, size_t n, size_t data_bytes
     uint64_t elems = 1;
     for (const JVal& d : sh->arr) {
       if (!integral(d)) return IE_ERR_INVALID_ARG;
+      const uint64_t dim = (uint64_t)d.num;
+      // a shape whose element count wraps around 64 bits could otherwise
+      // match a small (or empty) data range
+      if (dim != 0 && elems > UINT64_MAX / dim) return IE_ERR_INVALID_ARG;
       x.shape.push_back((int64_t)d.num);
-      elems *= (uint64_t)d.num;
+      elems *= dim;
     }
     x.begin = (uint64_t)off->arr[0].num;
     x.end = (uint64_t)off->arr[1].num;

@@ -40,7 +40,8 @@ struct Import {
   void* ptr;
   void* base;
 };
-Import g_imports[256];
+constexpr int kMaxImports = 256;
+Import g_imports[kMaxImports];
 int g_nimports = 0;
 
 }  // namespace
@@ -71,10 +72,12 @@ int ie_ipc_import(const void* handle, uint64_t offset, void** ptr_out) {
   cudaIpcMemHandle_t h;
   memcpy(&h, handle, sizeof(h));
   void* base = nullptr;
+  std::lock_guard<std::mutex> lock(g_import_mutex);
+  // every mapping must be releasable: refuse a new one when the table is full
+  if (g_nimports >= kMaxImports) return IE_ERR_UNSUPPORTED;
   if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return IE_ERR_UNSUPPORTED;
   *ptr_out = static_cast<char*>(base) + offset;
-  std::lock_guard<std::mutex> lock(g_import_mutex);
-  if (g_nimports < 256) g_imports[g_nimports++] = Import{*ptr_out, base};
+  g_imports[g_nimports++] = Import{*ptr_out, base};
   return IE_OK;
 }
 

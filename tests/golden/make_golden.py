@@ -98,4 +98,7 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    tree = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("INFENGINE_REF")
+    if not tree:
+        sys.exit("usage: make_golden.py <reference tree> (or set INFENGINE_REF)")
+    main(tree)

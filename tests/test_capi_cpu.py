@@ -127,6 +127,9 @@ def test_attention_rejects_bad_arguments_without_device(ie):
     assert call(ok(ldo=4000)) == -1                    # output row shorter than the heads
     assert call(ok(qhs=100 * 128)) == -1               # q head stride shorter than S rows
     assert call(ok(pos0=1900)) == -1                   # chunk runs past the cache (1900 + 300 > 2048)
+    big = 2**31 - 2                                    # pos0 + S would wrap a 32-bit int
+    assert call(ok(pos0=big, chs=1 << 62)) == -1
+    assert call(ok(pos0=big, S=16, chs=1 << 62)) == -1
     # ie_attention_decode(dt, R, rows_per_seq, nq, nkv, hd, q, q_hs, k, v, chs, cbs, cache_rows, positions,
     #                     pos0, out, ld_out, stream)
     dec = lambda R=1, rps=1, nq=32, nkv=8, rows=2048, pos0=0, k=f: lib.ie_attention_decode(
@@ -135,6 +138,7 @@ def test_attention_rejects_bad_arguments_without_device(ie):
     assert dec(R=3, rps=2) == -1                       # rows not a whole number of sequences
     assert dec(rows=4096) == -1                        # cache rows beyond the head stride
     assert dec(pos0=2048) == -1                        # position outside the cache
+    assert dec(R=2, pos0=2**31 - 1) == -1              # pos0 + R would wrap a 32-bit int
     assert dec(k=vp(0x1004)) == -2                     # cache not 16-byte aligned
     assert dec(R=0) == 0                               # no rows: no-op
 

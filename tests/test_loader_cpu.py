@@ -40,6 +40,8 @@ def _raw(path, header: bytes, data: bytes = b"\0" * 64):
     b'{"x": {"dtype": "BF16", "shape": [4]}}',                                     # no offsets
     b'{"x": {"dtype": "BF16", "shape": [-1], "data_offsets": [0, 2]}}',           # negative dimension
     b'[1, 2]',                                                                     # not an object
+    # an element count that wraps 64 bits to 0 must not match an empty range
+    b'{"x": {"dtype": "BF16", "shape": [4294967296, 4294967296], "data_offsets": [0, 0]}}',
 ])
 def test_bad_headers_rejected(tmp_path, header):
     from infengine_b200 import IEError
