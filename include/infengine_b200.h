@@ -63,6 +63,18 @@ const char* ie_version(void);
  * words to IE_OK. */
 int ie_device_status(int clear);
 
+/* Limit, in nanoseconds, of every bounded device-side wait on another party
+ * (a TMA copy or MMA inside the tensor-core kernels, a bulk copy inside the
+ * decode attention, another rank's rows inside ie_gemm_allreduce). On expiry
+ * the kernel records IE_ERR_TIMEOUT (see ie_device_status) and returns.
+ * ns = 0 restores the default of 2 s; at most 60 s (IE_ERR_INVALID_ARG
+ * above). Applies to the current device, to kernels that start after the
+ * call, and to graphs captured before it (the kernels read the limit when
+ * they run). A kernel that gives up still waits, for up to 2 s, for the copies
+ * and MMAs it issued itself before it exits. The reference has no
+ * counterpart (its kernels do not wait on one another). */
+int ie_set_wait_limit_ns(unsigned long long ns);
+
 /* ---- a1 / a5: projection GEMM --------------------------------------------
  * Replaces multiply_by_weight (kernels/ffn.cu:7-33, declared in
  * kernels/multiply_by_weight.cuh:3) and the O projection

@@ -59,6 +59,7 @@ EXPORTED_SYMBOLS = (
     "ie_attention_decode", "ie_gemm_add", "ie_gemm_allreduce_add", "ie_rmsnorm", "ie_embed", "ie_engine_create",
     "ie_engine_destroy", "ie_engine_prefill", "ie_engine_decode", "ie_engine_verify", "ie_engine_set_position",
     "ie_engine_position", "ie_engine_stream", "ie_engine_step", "ie_engine_create_tp", "ie_add_f32",
+    "ie_set_wait_limit_ns",
     "ie_st_open", "ie_st_close", "ie_st_count", "ie_st_name", "ie_st_info", "ie_llama_load", "ie_llama_model_desc",
     "ie_llama_model_shard", "ie_llama_model_free",
 )
@@ -86,6 +87,8 @@ def lib() -> ctypes.CDLL:
         L.ie_version.restype = ctypes.c_char_p
         L.ie_device_status.argtypes = [i32]
         L.ie_device_status.restype = i32
+        L.ie_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]
+        L.ie_set_wait_limit_ns.restype = i32
         L.ie_gemm.argtypes = [i32, i32, i32, i32, vp, i64, vp, i64, vp, i64, vp]
         L.ie_gemm_add.argtypes = [i32, i32, i32, i32, vp, i64, vp, i64, vp, i64, vp]
         L.ie_gemm_add.restype = i32
@@ -272,6 +275,12 @@ def argmax(logits, idx_out, stream=None):
 def device_status(clear: bool = True) -> int:
     """ie_device_status: IE_OK or IE_ERR_TIMEOUT from a bounded device wait."""
     return int(lib().ie_device_status(1 if clear else 0))
+
+
+def set_wait_limit_ns(ns: int = 0) -> None:
+    """ie_set_wait_limit_ns: limit of the kernels' bounded device-side waits
+    on the current device (0 restores the default of 2 s)."""
+    _check(lib().ie_set_wait_limit_ns(int(ns)), "ie_set_wait_limit_ns")
 
 
 def key_index(key: int) -> int:

@@ -51,13 +51,16 @@
 //    fixed rank order, so no rescaling of partial results is involved.
 //  * p.V partials ([group][128] fp32 per CTA) are summed across the cluster in
 //    rank order; each CTA rounds and stores 1/8 of the row's outputs.
-// Results are deterministic. Every mbarrier wait is bounded (2 s): on expiry
+// Results are deterministic. Every mbarrier wait is bounded (2 s unless
+// ie_set_wait_limit_ns says otherwise): on expiry
 // IE_ERR_TIMEOUT is recorded, no further copies are issued, the outstanding
 // ones are waited for (bounded) before the CTA exits, and the cluster
 // barriers are still passed by every CTA.
 namespace ie {
 
 __device__ int g_attn_status = 0;
+// limit of one bulk-copy wait (ie_set_wait_limit_ns)
+__device__ unsigned long long g_attn_wait_ns = kDefaultWaitNs;
 
 namespace {
 
@@ -66,7 +69,6 @@ constexpr int kFdWarps = kFdThreads / 32;
 constexpr int kFdRows = 64;
 constexpr int kFdStages = 6;
 constexpr int kFdRingBytes = kFdStages * kFdRows * 128 * 2;
-constexpr unsigned long long kFdWaitNs = 2000000000ull;
 
 struct FdParams {
   const void* q;
@@ -102,10 +104,11 @@ __device__ __forceinline__ unsigned long long fd_now() {
 // Bounded wait; false when it gave up or another thread already did.
 __device__ __forceinline__ bool fd_wait(uint32_t bar, uint32_t parity, volatile int* abort_s) {
   if (fd_try(bar, parity)) return true;
+  const unsigned long long limit = g_attn_wait_ns;
   const unsigned long long t0 = fd_now();
   while (!fd_try(bar, parity)) {
     if (*abort_s) return false;
-    if (fd_now() - t0 > kFdWaitNs) {
+    if (fd_now() - t0 > limit) {
       atomicExch(&g_attn_status, IE_ERR_TIMEOUT);
       *abort_s = 1;
       return false;
@@ -398,7 +401,7 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
     for (int i = fail_at; i < issued; ++i) {
       const unsigned long long t0 = fd_now();
       while (!fd_try(fd_smem_u32(&bars[i % kFdStages]), (uint32_t)((i / kFdStages) & 1)) &&
-             fd_now() - t0 < kFdWaitNs) {
+             fd_now() - t0 < kDrainWaitNs) {
       }
     }
   }
@@ -481,6 +484,10 @@ int fd_cluster_size(int n_kv_heads) {
 }
 
 }  // namespace
+
+cudaError_t set_attn_wait_ns(unsigned long long ns) {
+  return cudaMemcpyToSymbol(g_attn_wait_ns, &ns, sizeof(ns));
+}
 
 int read_attn_status(bool clear) {
   int v = 0;

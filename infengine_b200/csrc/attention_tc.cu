@@ -49,6 +49,8 @@
 namespace ie {
 
 __device__ int g_tca_status = 0;
+// limit of one mbarrier wait (ie_set_wait_limit_ns)
+__device__ unsigned long long g_tca_wait_ns = kDefaultWaitNs;
 
 namespace {
 
@@ -64,7 +66,6 @@ constexpr int kSBufs = 2;                    // S (then P) buffers in TMEM
 constexpr int kOCol = kSBufs * kBN;          // O accumulator columns [256, 384)
 constexpr int kQCol = kOCol + kD;            // Q (A operand of Q K^T), 64 columns
 constexpr uint32_t kTmemCols = 512;
-constexpr unsigned long long kWaitNs = 2000000000ull;
 // smem: K/V ring | cross-half row exchange | barriers
 constexpr int kOffRed = kStages * kTile;
 constexpr int kOffBars = kOffRed + 2 * kBM * 4;
@@ -82,7 +83,7 @@ struct TcaArgs {
 };
 
 __device__ __forceinline__ bool wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-  return tc::mbar_wait(bar, parity, abort_flag, &g_tca_status, kWaitNs);
+  return tc::mbar_wait(bar, parity, abort_flag, &g_tca_status, &g_tca_wait_ns);
 }
 
 // two fp32 values rounded to T (to nearest even) and packed, lo in bits 0-15
@@ -325,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
         // every MMA this thread issued finishes before TMEM is released
         mma_commit(drain_bar);
         const unsigned long long t0 = globaltimer();
-        while (!mbar_try(drain_bar, 0) && globaltimer() - t0 < kWaitNs) {
+        while (!mbar_try(drain_bar, 0) && globaltimer() - t0 < kDrainWaitNs) {
         }
       }
     }
@@ -467,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_attention_kernel(const __grid_
     const int issued = *issued_p;
     for (int t = max(0, issued - kStages); t < issued; ++t) {
       const unsigned long long t0 = globaltimer();
-      while (!mbar_try(full_bar(t % kStages), (uint32_t)((t / kStages) & 1)) && globaltimer() - t0 < kWaitNs / 4) {
+      while (!mbar_try(full_bar(t % kStages), (uint32_t)((t / kStages) & 1)) && globaltimer() - t0 < kDrainWaitNs / 4) {
       }
     }
   }
@@ -545,6 +546,10 @@ int launch_tc_attention(ie_dtype dt, int S, int pos0, int n_q_heads, int n_kv_he
   a.ld_out = ld_out;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return dt == IE_DTYPE_F16 ? launch<__half>(a, n_q_heads, st) : launch<__nv_bfloat16>(a, n_q_heads, st);
+}
+
+cudaError_t set_tca_wait_ns(unsigned long long ns) {
+  return cudaMemcpyToSymbol(g_tca_wait_ns, &ns, sizeof(ns));
 }
 
 int read_tca_status(bool clear) {

@@ -64,6 +64,15 @@ int ie_device_status(int clear) {
   return a != IE_OK ? a : (b != IE_OK ? b : (c != IE_OK ? c : (d != IE_OK ? d : e)));
 }
 
+int ie_set_wait_limit_ns(unsigned long long ns) {
+  if (ns > kMaxWaitNs) return IE_ERR_INVALID_ARG;
+  const unsigned long long v = ns ? ns : kDefaultWaitNs;
+  const cudaError_t e[4] = {set_tc_wait_ns(v), set_skinny_wait_ns(v), set_attn_wait_ns(v), set_tca_wait_ns(v)};
+  for (const cudaError_t x : e)
+    if (x != cudaSuccess) return IE_ERR_LAUNCH;
+  return IE_OK;
+}
+
 static int gemm_store(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw,
                       void* Y, int64_t ldy, bool residual, void* stream) {
   if (!valid_dtype(dt) || M < 0 || N < 0 || K <= 0) return IE_ERR_INVALID_ARG;

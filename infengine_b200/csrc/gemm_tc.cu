@@ -41,6 +41,8 @@
 namespace ie {
 
 __device__ int g_tc_status = 0;
+// limit of one mbarrier wait (ie_set_wait_limit_ns)
+__device__ unsigned long long g_tc_wait_ns = kDefaultWaitNs;
 
 namespace {
 
@@ -52,7 +54,6 @@ constexpr int TILE_BYTES = STAGES * STAGE_BYTES;  // 192 KB
 constexpr int SMEM_BYTES = TILE_BYTES + 1024 + 256;
 constexpr int THREADS = 192;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait
 
 struct TcArgs {
   CUtensorMap tmA;
@@ -65,7 +66,7 @@ struct TcArgs {
 // ------------------------------------------------------------ PTX helpers
 using namespace tc;
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-  return tc::mbar_wait(bar, parity, abort_flag, &g_tc_status, kWaitNs);
+  return tc::mbar_wait(bar, parity, abort_flag, &g_tc_status, &g_tc_wait_ns);
 }
 template <typename T>
 __device__ __forceinline__ uint32_t idesc_f16() {
@@ -240,7 +241,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
         // let every MMA this thread issued finish before TMEM is released
         mma_commit(drain_bar);
         const unsigned long long t0 = globaltimer();
-        while (!mbar_try(drain_bar, 0) && globaltimer() - t0 < kWaitNs) {
+        while (!mbar_try(drain_bar, 0) && globaltimer() - t0 < kDrainWaitNs) {
         }
       }
     }
@@ -404,7 +405,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
     const int issued = *issued_p, consumed = *consumed_p;
     for (int i = consumed; i < issued; ++i) {
       const unsigned long long t0 = globaltimer();
-      while (!mbar_try(full_bar(i % STAGES), (uint32_t)((i / STAGES) & 1)) && globaltimer() - t0 < kWaitNs / 4) {
+      while (!mbar_try(full_bar(i % STAGES), (uint32_t)((i / STAGES) & 1)) && globaltimer() - t0 < kDrainWaitNs / 4) {
       }
     }
   }
@@ -518,6 +519,10 @@ int launch_tc_gemm(ie_dtype dt, const TcGemmParams& p, cudaStream_t st) {
       return IE_ERR_UNSUPPORTED;
   }
   return dt == IE_DTYPE_BF16 ? dispatch<__nv_bfloat16>(a, p.epi, st) : dispatch<__half>(a, p.epi, st);
+}
+
+cudaError_t set_tc_wait_ns(unsigned long long ns) {
+  return cudaMemcpyToSymbol(g_tc_wait_ns, &ns, sizeof(ns));
 }
 
 int read_tc_status(bool clear) {

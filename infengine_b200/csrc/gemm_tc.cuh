@@ -55,5 +55,7 @@ int launch_tc_gemm(ie_dtype dt, const TcGemmParams& p, cudaStream_t st);
 
 // Device status word written by timed-out waits (IE_OK or IE_ERR_TIMEOUT).
 int read_tc_status(bool clear);
+// Sets this device's limit of the kernels' bounded waits (current device).
+cudaError_t set_tc_wait_ns(unsigned long long ns);
 
 }  // namespace ie

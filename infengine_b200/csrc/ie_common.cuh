@@ -77,6 +77,17 @@ __device__ __forceinline__ int argmax_key_index(unsigned long long key) {
   return (int)((tie & ((1u << 21) - 1u)) * 1024u + (__brev(tie >> 21) >> 22));
 }
 
+// ------------------------------------------------------------- waits
+// Limit of a device-side wait on another party (a TMA copy, an MMA, a peer
+// rank's data): 2 s unless ie_set_wait_limit_ns changes it. On expiry the
+// kernel records IE_ERR_TIMEOUT and returns. Waits for work the kernel itself
+// issued, when it leaves early (copies and MMAs in flight), keep the fixed
+// kDrainWaitNs: they always end, and cutting them short would let a CTA exit
+// with copies still landing in its shared memory.
+constexpr unsigned long long kDefaultWaitNs = 2000000000ull;
+constexpr unsigned long long kDrainWaitNs = 2000000000ull;
+constexpr unsigned long long kMaxWaitNs = 60000000000ull;  // largest settable limit: 60 s
+
 // ------------------------------------------------------------- misc
 __host__ __device__ __forceinline__ int ceil_div(int a, int b) { return (a + b - 1) / b; }
 

@@ -116,6 +116,8 @@ __device__ __forceinline__ const T* weight_row(const SkinnyParams& p, int tile, 
 // for another rank's rows gave up, IE_ERR_INVALID_ARG when a batched QKV row
 // carried a position outside its cache.
 __device__ int g_skinny_status = 0;
+// limit of the wait for other ranks' rows (ie_set_wait_limit_ns)
+__device__ unsigned long long g_skinny_wait_ns = kDefaultWaitNs;
 
 // Epilogues, run by warp 0 on the fully reduced tile.
 // acc[.][mt][i]: weight row g + 8*(i>>1) of the tile, batch row m = mt*8 + 2t + (i&1).
@@ -159,6 +161,7 @@ __device__ __forceinline__ void epilogue(const SkinnyParams& p, int tile, int g,
                                           static_cast<const char*>(p.tp_sym[p.tp_rank]) + kTpInboxOffset) +
                                       base;
     T* Y = static_cast<T*>(p.Y);
+    const unsigned long long limit = g_skinny_wait_ns;
     unsigned long long t0;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
     bool gave_up = false;
@@ -180,7 +183,7 @@ __device__ __forceinline__ void epilogue(const SkinnyParams& p, int tile, int g,
             }
             unsigned long long now;
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-            if (now - t0 > 2000000000ull) {
+            if (now - t0 > limit) {
               atomicExch(&g_skinny_status, IE_ERR_TIMEOUT);
               gave_up = true;
               break;
@@ -701,6 +704,10 @@ cudaError_t launch_skinny(ie_dtype dt, int epi, const SkinnyParams& p, cudaStrea
   else { IE_SK(__nv_bfloat16) }
 #undef IE_SK
   return cudaErrorInvalidValue;
+}
+
+cudaError_t set_skinny_wait_ns(unsigned long long ns) {
+  return cudaMemcpyToSymbol(g_skinny_wait_ns, &ns, sizeof(ns));
 }
 
 int read_skinny_status(bool clear) {

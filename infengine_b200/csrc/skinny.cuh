@@ -79,6 +79,8 @@ cudaError_t launch_swiglu(ie_dtype dt, int64_t n, const void* gate, const void* 
 // Device status word of the decode kernels (IE_OK, IE_ERR_TIMEOUT from the
 // tensor-parallel exchange, IE_ERR_INVALID_ARG from a batched QKV position).
 int read_skinny_status(bool clear);
+// Sets this device's limit of the kernels' bounded waits (current device).
+cudaError_t set_skinny_wait_ns(unsigned long long ns);
 cudaError_t launch_argmax(ie_dtype dt, int M, int V, const void* logits, int64_t ld, int* idx_out, cudaStream_t st);
 
 }  // namespace ie

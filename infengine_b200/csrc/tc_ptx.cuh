@@ -36,12 +36,13 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait on an mbarrier phase: false when it gave up after wait_ns
+// Bounded wait on an mbarrier phase: false when it gave up after *wait_ns_p
 // (IE_ERR_TIMEOUT recorded in *status, abort raised) or when another role
 // already raised the abort flag.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
-                                          unsigned long long wait_ns) {
+                                          const unsigned long long* wait_ns_p) {
   if (mbar_try(bar, parity)) return true;
+  const unsigned long long wait_ns = *wait_ns_p;
   const unsigned long long t0 = globaltimer();
   while (true) {
     if (mbar_try(bar, parity)) return true;

@@ -103,6 +103,8 @@ def test_invalid_arguments_rejected_without_device(ie):
                                  None) == -3
     # argmax leading dimension smaller than V
     assert lib.ie_argmax(0, 1, 100, fake, 50, fake, None) == -1
+    # wait limit above the 60 s ceiling (checked before the device is touched)
+    assert lib.ie_set_wait_limit_ns(61 * 10**9) == -1
 
 
 def test_attention_rejects_bad_arguments_without_device(ie):
