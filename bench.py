@@ -611,6 +611,271 @@ def reference_decode(seed, steps, warmup):
     return {"decode_ms": dm.value, "prefill_ms": pm.value, "tokens": out}
 
 
+# ------------------------------------- the reference's kernels, per config
+def reference_configs(torch, dev, seed):
+    """Baseline leg, not part of our path: the reference's own hot-path code
+    (kernels/ffn.cu, attn.cu, lm_head.cu, swiglu.cu, rope.cu, sampling.cu with
+    cuBLAS 12.9, built unchanged for sm_100a by oracle/Makefile) at BASELINE
+    configs 1-4, in fp16 (its only dtype), launched eagerly on the legacy
+    default stream as the reference launches them, timed with CUDA events on
+    that stream. Weights: the same seeded random-init model (bf16 values
+    stored as fp16), each kernel timed over the 32 layers' copies (or 4 lm_head
+    launches), so weights stream from HBM. Each prefill entry gives the cuBLAS
+    calls alone (`gemm_us`) and with the elementwise kernels the reference
+    runs right after them (`path_us`: RoPE after Q/K/V, SwiGLU after gate and
+    up), which our fused kernels fold into their epilogues."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    from ref_lib import p, ref
+    from infengine_b200.host import rope_tables
+    R = ref()
+    R.ref_set_stream(None)
+    f16 = torch.float16
+    layers, lm = make_weights(torch, dev, f16, seed)
+    ds = torch.cuda.default_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed_eager(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        e0.record(ds)
+        for _ in range(reps):
+            fn()
+        e1.record(ds)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / reps
+
+    out = {}
+    x1, y1 = torch.randn(1, H, device=dev).to(f16), torch.empty(1, H, device=dev, dtype=f16)
+    t = timed_eager(lambda: [R.ref_multiply_by_weight(1, H, H, p(x1), p(w["wo"]), p(y1)) for w in layers], 5) / L
+    b = 2 * (H * H + 2 * H)
+    out["c1_gemv_4096x4096"] = {"us": round(t * 1e6, 2), "gbs": round(b / t / 1e9, 1), "call": "multiply_by_weight"}
+    c2 = {}
+    for m in (1, 4, 8):
+        xm, om = torch.randn(m, H, device=dev).to(f16), torch.empty(m, H, device=dev, dtype=f16)
+        ws = torch.empty(R.ref_ffn_workspace_size(m), dtype=torch.uint8, device=dev)
+        t = timed_eager(lambda: [R.ref_ffn(m, p(xm), p(om), p(w["wu"]), p(w["wd"]), p(w["wg"]), p(ws))
+                                 for w in layers], 5) / L
+        b = 2 * (3 * F * H + 2 * m * H)
+        c2[f"m{m}"] = {"us": round(t * 1e6, 2), "gbs": round(b / t / 1e9, 1)}
+    out["c2_ffn_decode"] = dict(c2, call="ffn (3 cuBLAS GEMMs + swiglu)")
+    c4 = {}
+    for B in (1, 8, 64):
+        xb = torch.randn(B, H, device=dev).to(f16)
+        logits = torch.empty(B, V, device=dev, dtype=f16)
+        tok = torch.zeros(B, dtype=torch.int32, device=dev)
+        if B == 1:  # lm_head (its row seq_len - 1) + sample_token_amax, as decode.cu:41-42
+            fn = lambda: [(R.ref_lm_head(1, p(xb), p(lm), p(logits)), R.ref_sample_token_amax(p(logits), p(tok)))
+                          for _ in range(4)]
+        else:  # no batched lm_head in the reference: one GEMM over B rows + amax per row
+            fn = lambda: [(R.ref_multiply_by_weight(B, H, V, p(xb), p(lm), p(logits)),
+                           [R.ref_sample_token_amax(ctypes_ptr(logits, r * V), ctypes_ptr(tok, r)) for r in range(B)])
+                          for _ in range(4)]
+        t = timed_eager(fn, 2) / 4
+        b = 2 * (V * H + B * H)
+        c4[f"b{B}"] = {"us": round(t * 1e6, 2), "gbs": round(b / t / 1e9, 1)}
+    out["c4_lm_head_argmax"] = dict(c4, call="lm_head + sample_token_amax (B=1); multiply_by_weight + B x "
+                                             "sample_token_amax (B>1)")
+    S = 2048
+    xs = torch.randn(S, H, device=dev).to(f16)
+    hs = torch.randn(S, F, device=dev).to(f16)
+    q = torch.empty(NQ, S, HD, device=dev, dtype=f16)
+    kc, vc = (torch.zeros(NKV, CTX, HD, device=dev, dtype=f16) for _ in range(2))
+    G, U = torch.empty(S, F, device=dev, dtype=f16), torch.empty(S, F, device=dev, dtype=f16)
+    o = torch.empty(S, H, device=dev, dtype=f16)
+    cos, sin = (torch.from_numpy(a).to(dev) for a in rope_tables(CTX))
+
+    def qkv(w, rope):
+        R.ref_qkv_proj(S, p(xs), p(w["wq"]), p(w["wk"]), p(w["wv"]), p(q), p(kc), p(vc), NQ, NKV)
+        if rope:  # attn.cu:351-352
+            R.ref_apply_rope(0, NKV, S, p(cos), p(sin), p(kc), 1)
+            R.ref_apply_rope(0, NQ, S, p(cos), p(sin), p(q), 0)
+
+    def gate_up(w, act):
+        R.ref_multiply_by_weight(S, H, F, p(xs), p(w["wg"]), p(G))
+        R.ref_multiply_by_weight(S, H, F, p(xs), p(w["wu"]), p(U))
+        if act:  # ffn.cu:57
+            R.ref_swiglu(S, p(G), p(U), p(G))
+
+    c3 = {}
+    for name, gemm, path, flops in (
+        ("qkv_6144x4096", lambda: [qkv(w, False) for w in layers], lambda: [qkv(w, True) for w in layers],
+         2 * S * 6144 * H),
+        ("o_4096x4096", lambda: [R.ref_o_proj(S, p(xs), p(w["wo"]), p(o)) for w in layers], None, 2 * S * H * H),
+        ("gate_up_2x14336x4096", lambda: [gate_up(w, False) for w in layers], lambda: [gate_up(w, True) for w in layers],
+         2 * S * 2 * F * H),
+        ("down_4096x14336", lambda: [R.ref_multiply_by_weight(S, F, H, p(hs), p(w["wd"]), p(o)) for w in layers], None,
+         2 * S * H * F),
+    ):
+        tg = timed_eager(gemm, 2) / L
+        tp = timed_eager(path, 2) / L if path is not None else tg
+        c3[name] = {"gemm_us": round(tg * 1e6, 1), "gemm_tflops": round(flops / tg / 1e12, 1),
+                    "path_us": round(tp * 1e6, 1), "path_tflops": round(flops / tp / 1e12, 1)}
+    out["c3_prefill_m2048"] = c3
+    out["timing"] = ("eager on the legacy default stream (the reference's launch mode), CUDA events; fp16; weights "
+                     "rotated over the 32 layers' copies")
+    del layers, lm
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
+
+
+def ctypes_ptr(t, offset_elems):
+    import ctypes
+    return ctypes.c_void_p(t.data_ptr() + offset_elems * t.element_size())
+
+
+def versus_reference(ours, ref):
+    """Speed-up of our per-config times over the reference's (same box)."""
+    def r(a, b):
+        return round(b / a, 3) if a and b else None
+    vs = {"c1_gemv_4096x4096": r(ours["c1_gemv_4096x4096"]["us"], ref["c1_gemv_4096x4096"]["us"])}
+    vs["c2_ffn_decode"] = {k: r(ours["c2_ffn_decode"][k]["us"], ref["c2_ffn_decode"][k]["us"]) for k in ("m1", "m4", "m8")}
+    vs["c4_lm_head_argmax"] = {k: r(ours["c4_lm_head_argmax"][k]["us"], ref["c4_lm_head_argmax"][k]["us"])
+                               for k in ("b1", "b8", "b64")}
+    vs["c3_prefill_m2048"] = {
+        k: {"vs_path": r(ours["c3_prefill_m2048"][k]["us"], ref["c3_prefill_m2048"][k]["path_us"]),
+            "vs_gemm_only": r(ours["c3_prefill_m2048"][k]["us"], ref["c3_prefill_m2048"][k]["gemm_us"])}
+        for k in ours["c3_prefill_m2048"]}
+    return vs
+
+
+# ----------------------------------------------------------- parity checker
+def fp16_spacing(x: float) -> float:
+    """Spacing of fp16 numbers at |x| (one unit in the last place)."""
+    import math
+    a = max(abs(x), 2.0 ** -14)
+    return 2.0 ** (math.floor(math.log2(a)) - 10)
+
+
+def parity_leg(torch, dev, seed, n_steps, batch=8):
+    """Checker leg (untimed): greedy ids of BASELINE config 5 at its full
+    length against the reference's own decode loop.
+
+    The reference (prefill.cu / decode.cu with its kernels and cuBLAS, built
+    unchanged by oracle/Makefile; manager.cpp:79-86's loop) runs on its
+    random-init fp16 model, once per prompt: PROMPT tokens, then n_steps
+    greedy ids, with its top-2 logit margin and top logit at every step. Our
+    engine runs in fp16 on the same weights:
+      * bs1 - teacher-forced (each step fed the reference's previous id, so
+        every step is scored on the same context) and free-running;
+      * bs8 - `batch` prompts decoded together, each against its own bs1
+        reference run;
+      * verify M=5 - one verify pass over the reference's ids 0..4, compared
+        with its ids 1..5.
+    Every disagreement is listed with the reference's margin in fp16 units of
+    its top logit."""
+    import ctypes
+    from infengine_b200.engine import LlamaEngine
+    vp, i32 = ctypes.c_void_p, ctypes.c_int
+    R = ctypes.CDLL(str(ROOT / "oracle" / "_ref" / "libref_model_ref.so"))
+    R.model_init.argtypes = [ctypes.c_ulonglong]
+    R.model_generate_ex.argtypes = [vp, i32, i32, vp, vp, vp, vp, vp, vp]
+    R.model_weight_ptrs.argtypes = [vp, i32]
+    t_start = time.perf_counter()
+    assert R.model_init(seed) == 0
+    ps = prompts(seed, batch)  # the prompts of the timed runs (bs1 uses the first)
+    ref_ids, ref_m, ref_top = [], [], []
+    for b in range(batch):
+        ids, m, top = np.zeros(n_steps, np.int32), np.zeros(n_steps, np.float32), np.zeros(n_steps, np.float32)
+        assert R.model_generate_ex(ps[b].ctypes.data_as(vp), PROMPT, n_steps, None, ids.ctypes.data_as(vp),
+                                   m.ctypes.data_as(vp), top.ctypes.data_as(vp), None, None) == 0
+        ref_ids.append(ids)
+        ref_m.append(m)
+        ref_top.append(top)
+    n = 5 + 9 * L
+    ptrs = (ctypes.c_void_p * n)()
+    assert R.model_weight_ptrs(ptrs, n) == n
+    v = [int(x) for x in ptrs]
+    names = ["attn_norm", "wq", "wk", "wv", "wo", "ffn_norm", "w_gate", "w_up", "w_down"]
+    weights = dict(embedding=v[0], final_norm=v[1], lm_head=v[2], rope_cos=v[3], rope_sin=v[4],
+                   layers=[dict(zip(names, v[5 + 9 * l: 14 + 9 * l])) for l in range(L)])
+    dims = dict(n_layers=L, hidden=H, n_q_heads=NQ, n_kv_heads=NKV, head_dim=HD, ffn_dim=F, vocab=V, rms_eps=1e-5)
+
+    def misses(seq, got):
+        bad = np.nonzero(got != ref_ids[seq])[0]
+        return [{"seq": seq, "step": int(i), "ref_margin": float(ref_m[seq][i]), "ref_top": float(ref_top[seq][i]),
+                 "margin_in_ulps": round(float(ref_m[seq][i]) / fp16_spacing(float(ref_top[seq][i])), 2)}
+                for i in bad]
+
+    def first_difference(a, b):
+        d = np.nonzero(a != b)[0]
+        return int(d[0]) if len(d) else len(a)
+
+    out = {"checker": "the reference's decode loop (prefill.cu, decode.cu, kernels/*.cu + cuBLAS 12.9, compiled "
+                      "unchanged for sm_100a) on its random-init fp16 model; ours: the decode engine in fp16 on the "
+                      "same weights", "prompt": PROMPT, "steps": n_steps}
+    try:
+        eng = LlamaEngine(weights, dims, dtype="f16", max_batch=1, max_ctx=PROMPT + n_steps + 8, max_prefill=PROMPT)
+        r0 = ref_ids[0]
+        first = eng.prefill(0, ps[0])
+        tf = [first]
+        for i in range(n_steps - 1):
+            eng.set_position(0, PROMPT + i, int(r0[i]))
+            tf.append(int(eng.decode(1)[0, 0]))
+        tf = np.array(tf, np.int32)
+        eng.set_position(0, PROMPT, first)
+        free = np.concatenate([[first], eng.decode(n_steps - 1)[:, 0]]).astype(np.int32)
+        eng.set_position(0, PROMPT, int(r0[0]))
+        ver = eng.verify(0, r0[:5])
+        eng.close()
+        m1 = misses(0, tf)
+        out["bs1"] = {"teacher_forced_equal": int((tf == r0).sum()), "of": n_steps,
+                      "free_running_identical_steps": first_difference(free, r0), "misses": m1}
+        out["verify_m5"] = {"equal": int((ver == r0[1:6]).sum()), "of": 5, "ids": ver.tolist(),
+                            "reference": r0[1:6].tolist()}
+        eng = LlamaEngine(weights, dims, dtype="f16", max_batch=batch, max_ctx=PROMPT + n_steps + 8,
+                          max_prefill=PROMPT)
+        firsts = [eng.prefill(b, ps[b]) for b in range(batch)]
+        tf8 = np.zeros((n_steps, batch), np.int32)
+        tf8[0] = firsts
+        for i in range(n_steps - 1):
+            for b in range(batch):
+                eng.set_position(b, PROMPT + i, int(ref_ids[b][i]))
+            tf8[i + 1] = eng.decode(1)[0]
+        for b in range(batch):
+            eng.set_position(b, PROMPT, firsts[b])
+        free8 = np.concatenate([np.array(firsts, np.int32)[None], eng.decode(n_steps - 1)]).astype(np.int32)
+        eng.close()
+        m8 = [x for b in range(batch) for x in misses(b, tf8[:, b])]
+        out["bs8"] = {"teacher_forced_equal": int(sum((tf8[:, b] == ref_ids[b]).sum() for b in range(batch))),
+                      "of": n_steps * batch,
+                      "free_running_identical_steps": [first_difference(free8[:, b], ref_ids[b]) for b in range(batch)],
+                      "bs8_row0_equals_bs1_free_run": bool(np.array_equal(free8[:, 0], free)),
+                      "misses": m8}
+        allm = m1 + m8
+        out["max_miss_margin_ulps"] = max((x["margin_in_ulps"] for x in allm), default=None)
+    finally:
+        R.model_free()
+    out["seconds"] = round(time.perf_counter() - t_start, 1)
+    return out
+
+
+def tp_parity(torch, dist, dev, seed, rank, prompt, tp_ids, ctx):
+    """Rank 0 (untimed, after the timed steps): the single-GPU engine on the
+    full model from the same seeded generator, prefill of the same prompt and
+    as many greedy steps; its ids against the tensor-parallel engine's ids of
+    the run (prefill id, warm-up steps, timed steps). The other ranks wait."""
+    res = None
+    if rank == 0:
+        layers, lm = make_weights(torch, dev, torch.bfloat16, seed)
+        weights = full_model_weights(torch, dev, seed, layers, lm)
+        eng = make_engine(weights, 1, 0, 1, ctx)
+        eng.prefill(0, prompt[:256])  # the same warm-up the TP run made
+        eng.set_position(0, 0, 0)
+        first = eng.prefill(0, prompt)
+        ids = np.concatenate([[first], eng.decode(len(tp_ids) - 1)[:, 0]]).astype(np.int32)
+        eng.close()
+        del eng, weights, layers, lm
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        d = np.nonzero(ids != tp_ids)[0]
+        res = {"ids": len(tp_ids), "equal": int((ids == tp_ids).sum()), "identical": bool(len(d) == 0),
+               "first_difference": int(d[0]) if len(d) else None,
+               "against": "single-GPU engine, same seeded bf16 model and prompt"}
+    dist.barrier()
+    return res
+
+
 # ------------------------------------------------------------------- main
 def timed(torch, stream, fn, world, dev):
     """Device time (ms) of fn() on `stream`, max over ranks."""
@@ -640,6 +905,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--parity-steps", type=int, default=256,
+                    help="greedy steps of the parity checker leg (N=1; 0 skips it)")
+    ap.add_argument("--no-reference-configs", action="store_true",
+                    help="skip timing the reference's own kernels per BASELINE config")
     ap.add_argument("--case", default=None,
                     help="for profiling: one kernel (gate_up|down|o|qkv|lm_head|prefill_{qkv,o,gate_up,down}|"
                          "prefill_attention) "
@@ -729,6 +998,10 @@ def run_reference(torch, dev, args):
     result["matmul_path"] = {"tok_per_s": round(1e3 / ms_mm, 3), "ms_per_step": round(ms_mm, 4),
                              "hbm_gbs_per_gpu": round(WEIGHT_BYTES / (ms_mm / 1e3) / 1e9, 1)}
     del step
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    if not args.no_reference_configs:
+        result["configs"] = reference_configs(torch, dev, args.seed)
     if not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args.seed)
     emit(result)
@@ -759,14 +1032,16 @@ def run_ours(torch, dist, dev, args, world, rank, local, hbm_peak, tf_peak, tf_p
     t0 = time.perf_counter()
     first = eng.prefill(0, prompt)
     prefill_s = time.perf_counter() - t0
-    eng.decode(args.warmup)  # captures the step graph, then replays it
+    warm_ids = eng.decode(args.warmup)  # captures the step graph, then replays it
 
     # ---------------- timed region: K decode steps (graph replays), device events
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    ms_total = timed(torch, es, lambda: eng.decode(args.steps), world, dev)
+    timed_ids = {}
+    ms_total = timed(torch, es, lambda: timed_ids.__setitem__("ids", eng.decode(args.steps)), world, dev)
     clk = clocks.stop()
+    run_ids = np.concatenate([[first], warm_ids[:, 0], timed_ids["ids"][:, 0]]).astype(np.int32)
     ms_step = ms_total / args.steps
     tok_s = args.steps / (ms_total / 1e3)
 
@@ -793,6 +1068,9 @@ def run_ours(torch, dist, dev, args, world, rank, local, hbm_peak, tf_peak, tf_p
     eng.close()
     del eng, es
     torch.cuda.synchronize()
+    if world > 1:
+        # the N-rank engine's ids of this run against the single-GPU engine's
+        result["tp_parity"] = tp_parity(torch, dist, dev, args.seed, rank, prompt, run_ids, ctx)
 
     # ---------------- the weight-matmul path alone (north-star target: >= 80 % of HBM)
     graph = torch.cuda.CUDAGraph()
@@ -877,6 +1155,10 @@ def run_ours(torch, dist, dev, args, world, rank, local, hbm_peak, tf_peak, tf_p
         # BASELINE configs 1-4 one by one (before the long prefill chain, which
         # leaves the GPU warm and power-capped)
         result["configs"] = per_config(torch, step, stream, hbm_peak, tf_peak)
+        if not args.no_reference_configs:
+            ref_cfg = reference_configs(torch, dev, args.seed)
+            result["configs_reference"] = ref_cfg
+            result["configs_speedup_vs_reference"] = versus_reference(result["configs"], ref_cfg)
         gp = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
             step.prefill()
@@ -935,6 +1217,10 @@ def run_ours(torch, dist, dev, args, world, rank, local, hbm_peak, tf_peak, tf_p
                                "timing": "device events around blocking ie_engine_verify calls (host ids out)"}
         eng5.close()
         del eng5, es5
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        if args.parity_steps > 0:
+            result["parity"] = parity_leg(torch, dev, args.seed, args.parity_steps)
         if not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(args.seed)
 

@@ -130,12 +130,12 @@ REF_API int model_weight_ptrs(void** out, int n) {
 // forced[i] instead of the model's own pick (teacher forcing); out_tokens[i]
 // is always the model's pick. out_margin[i] (nullable): top-1 minus top-2
 // logit of step i (fp16 logits read back).
-REF_API int model_generate_timed(const int* prompt, int n_prompt, int n_new, const int* forced, int* out_tokens,
-                                 float* out_margin, double* prefill_ms, double* decode_ms);
+REF_API int model_generate_ex(const int* prompt, int n_prompt, int n_new, const int* forced, int* out_tokens,
+                              float* out_margin, float* out_top, double* prefill_ms, double* decode_ms);
 
 REF_API int model_generate(const int* prompt, int n_prompt, int n_new, const int* forced, int* out_tokens,
                            float* out_margin) {
-  return model_generate_timed(prompt, n_prompt, n_new, forced, out_tokens, out_margin, nullptr, nullptr);
+  return model_generate_ex(prompt, n_prompt, n_new, forced, out_tokens, out_margin, nullptr, nullptr, nullptr);
 }
 
 // As model_generate; prefill_ms / decode_ms (nullable) receive the host wall
@@ -144,6 +144,14 @@ REF_API int model_generate(const int* prompt, int n_prompt, int n_new, const int
 // With out_margin set the margin read-backs fall inside the decode time.
 REF_API int model_generate_timed(const int* prompt, int n_prompt, int n_new, const int* forced, int* out_tokens,
                                  float* out_margin, double* prefill_ms, double* decode_ms) {
+  return model_generate_ex(prompt, n_prompt, n_new, forced, out_tokens, out_margin, nullptr, prefill_ms, decode_ms);
+}
+
+// As model_generate_timed; out_top (nullable, n_new entries) receives the
+// largest fp16 logit of each step, so a margin can be expressed in units of
+// the fp16 spacing at the top logit.
+REF_API int model_generate_ex(const int* prompt, int n_prompt, int n_new, const int* forced, int* out_tokens,
+                              float* out_margin, float* out_top, double* prefill_ms, double* decode_ms) {
   int* tokenid_buff;
   half *data_buffer, *aux_buffer, *attn_buffer, *output_distr;
   int* output_token;
@@ -160,6 +168,7 @@ REF_API int model_generate_timed(const int* prompt, int n_prompt, int n_new, con
   cudaMalloc(&kv_cache, kv_cache_size());
   cudaMemset(kv_cache, 0, kv_cache_size());
   std::vector<half> logits(VOCAB_SIZE);
+  float top = 0.f;
   auto margin = [&]() {
     cudaMemcpy(logits.data(), output_distr, VOCAB_SIZE * sizeof(half), cudaMemcpyDeviceToHost);
     float a = -INFINITY, b = -INFINITY;
@@ -167,6 +176,7 @@ REF_API int model_generate_timed(const int* prompt, int n_prompt, int n_new, con
       const float v = __half2float(logits[i]);
       if (v > a) { b = a; a = v; } else if (v > b) b = v;
     }
+    top = a;
     return a - b;
   };
   int seq_len = n_prompt;
@@ -178,7 +188,11 @@ REF_API int model_generate_timed(const int* prompt, int n_prompt, int n_new, con
   const auto t1 = std::chrono::steady_clock::now();
   for (int i = 0; i < n_new; ++i) {
     out_tokens[i] = tok;
-    if (out_margin) out_margin[i] = margin();
+    if (out_margin || out_top) {
+      const float m = margin();
+      if (out_margin) out_margin[i] = m;
+      if (out_top) out_top[i] = top;
+    }
     if (i + 1 == n_new) break;
     const int next = forced ? forced[i] : tok;
     cudaMemcpy(tokenid_buff + seq_len, &next, sizeof(int), cudaMemcpyHostToDevice);

@@ -173,24 +173,40 @@ def test_lm_head_argmax(ie, cuda, dt, M):
             assert top2[1] - top2[0] <= 2 * ulp(top2[1:], dt)[0]
 
 
-def test_lm_head_vocab_shards_merge_by_key_max(ie, cuda):
-    """Vocab split across 4 shards (TP=4 layout): max of packed keys = full argmax."""
-    dt, M, K, V = "bf16", 3, 4096, 128256
-    d = oracle.seeded_inputs(5, {"x": (M, K), "w": (V, K)}, dt)
-    T = torch_dtype(dt)
+@pytest.mark.parametrize("n_shards", [2, 4, 8])
+@pytest.mark.parametrize("M", [3, 64])
+def test_lm_head_vocab_shards_merge_by_key_max(ie, cuda, n_shards, M):
+    """Vocabulary split as tensor parallelism splits it at 2 / 4 / 8 ranks
+    (64128 / 32064 / 16032 rows per shard; 16032 is not a multiple of the
+    tensor-core kernel's 128-row tiles), on the decode kernel (M = 3) and the
+    tensor-core kernel (M = 64): the max of the shards' packed keys is the
+    full-vocabulary id. Each row's winning weight row is first copied into
+    the next shard at the same offset, so the merge also has to resolve
+    exact cross-shard ties in the reference's order."""
+    dt, K, V = "bf16", 4096, 128256
+    d = oracle.seeded_inputs(5 + M, {"x": (M, K), "w": (V, K)}, dt)
     x, w = to_dev(d["x"], dt), to_dev(d["w"], dt)
     ws = cuda.zeros(ie.lm_head_workspace_bytes(M), dtype=cuda.uint8, device="cuda")
+    shard = V // n_shards
     full_idx = cuda.empty((M,), dtype=cuda.int32, device="cuda")
     ie.lm_head_argmax(x, w, ws, idx_out=full_idx)
-    shard = V // 4
+    for i in set(full_idx.cpu().tolist()):  # plant the ties
+        w[(i + shard) % V] = w[i]
+    logits = cuda.empty((M, V), dtype=cuda.bfloat16, device="cuda")
+    ie.lm_head_argmax(x, w, ws, logits=logits, idx_out=full_idx)
     keys = []
-    for s in range(4):
+    for s in range(n_shards):
         k = cuda.zeros((M,), dtype=cuda.int64, device="cuda")
         ie.lm_head_argmax(x, w[s * shard:(s + 1) * shard], ws, key_out=k, vocab_offset=s * shard)
         keys.append(k.cpu().numpy().view(np.uint64))
+    cuda.cuda.synchronize()
     merged = np.max(np.stack(keys), axis=0)
+    got_logits = from_dev(logits)
     for m in range(M):
-        assert ie.key_index(int(merged[m])) == int(full_idx[m].item())
+        want = int(full_idx[m].item())
+        assert want == oracle.argmax_reference_fast(got_logits[m])
+        assert ie.key_index(int(merged[m])) == want, (m, want)
+    assert int(ws.sum().item()) == 0
 
 
 GOLD_AMAX = 75177  # tests/golden/reference_golden.json

@@ -41,10 +41,13 @@ def _bind(ie):
     return L
 
 
+IE_DTYPE_BF16 = 1
+
+
 def _call(L, x, w, y, desc):
     M, K = x.shape
     N = w.shape[0]
-    return L.ie_gemm_allreduce(2, M, N, K, x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), y.data_ptr(),
+    return L.ie_gemm_allreduce(IE_DTYPE_BF16, M, N, K, x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), y.data_ptr(),
                                y.stride(0), ctypes.byref(desc), None)
 
 
