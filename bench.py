@@ -205,19 +205,23 @@ class OursStep:
         self.ap = torch.empty(S, H, device=dev, dtype=torch.bfloat16)
         self.hp = torch.empty(S, F, device=dev, dtype=torch.bfloat16)
         self.op = torch.empty(S, H, device=dev, dtype=torch.bfloat16)
+        self.split_ws = self.ie.split_workspace(dev)  # the tail split of the *_ws entry points
 
     def release_prefill(self):
-        self.xp = self.qp = self.ap = self.hp = self.op = None
+        self.xp = self.qp = self.ap = self.hp = self.op = self.split_ws = None
 
-    def prefill(self):
-        """32 x [fused QKV+RoPE, O, gate/up+SwiGLU, down] at M = S tokens (positions 0..S-1)."""
+    def prefill(self, workspace="split"):
+        """32 x [fused QKV+RoPE, O, gate/up+SwiGLU, down] at M = S tokens
+        (positions 0..S-1), with the tail split (the engine's prefill path)
+        or, workspace=None, whole tiles only."""
         ie, S = self.ie, self.S
+        ws = self.split_ws if workspace == "split" else None
         for l, w in enumerate(self.layers):
             ie.qkv(self.xp, w["wq"], w["wk"], w["wv"], self.qp, self.kc[l], self.vc[l], CTX * HD, 0, self.cos,
-                   self.sin)
-            ie.gemm(self.qp.view(S, H), w["wo"], self.ap)  # stand-in for the attention output
-            ie.ffn_gate_up(self.xp, w["wg"], w["wu"], self.hp)
-            ie.gemm(self.hp, w["wd"], self.op)
+                   self.sin, workspace=ws)
+            ie.gemm(self.qp.view(S, H), w["wo"], self.ap, workspace=ws)  # stand-in for the attention output
+            ie.ffn_gate_up(self.xp, w["wg"], w["wu"], self.hp, workspace=ws)
+            ie.gemm(self.hp, w["wd"], self.op, workspace=ws)
 
     def prefill_flops(self):
         return 2.0 * self.S * L * LAYER_WEIGHT_ELEMS
@@ -392,20 +396,27 @@ def per_config(torch, step, stream, hbm_peak, tf_peak):
         c4[f"b{B}"] = {"us": round(t * 1e6, 2), "gbs": round(b / t / 1e9, 1), "frac_hbm": round(b / t / 1e9 / hbm_peak, 4),
                        "tflops": round(2 * B * V * H / t / 1e12, 2)}
     out["c4_lm_head_argmax"] = c4
-    # config 3: each prefill projection at M=2048 over the 32 layers
+    # config 3: each prefill projection at M=2048 over the 32 layers, with
+    # the tail split (the engine's path) and with whole tiles only
     S = step.S
     c3 = {}
-    for name, fn, flops in (
-        ("qkv_6144x4096", lambda: [ie.qkv(step.xp, w["wq"], w["wk"], w["wv"], step.qp, step.kc[l], step.vc[l], CTX * HD,
-                                          0, step.cos, step.sin) for l, w in enumerate(Ls)], 2 * S * 6144 * H),
-        ("o_4096x4096", lambda: [ie.gemm(step.qp.view(S, H), w["wo"], step.ap) for w in Ls], 2 * S * H * H),
-        ("gate_up_2x14336x4096", lambda: [ie.ffn_gate_up(step.xp, w["wg"], w["wu"], step.hp) for w in Ls],
-         2 * S * 2 * F * H),
-        ("down_4096x14336", lambda: [ie.gemm(step.hp, w["wd"], step.op) for w in Ls], 2 * S * H * F),
-    ):
+
+    def c3_cases(ws):
+        return (
+            ("qkv_6144x4096", lambda: [ie.qkv(step.xp, w["wq"], w["wk"], w["wv"], step.qp, step.kc[l], step.vc[l],
+                                              CTX * HD, 0, step.cos, step.sin, workspace=ws) for l, w in enumerate(Ls)],
+             2 * S * 6144 * H),
+            ("o_4096x4096", lambda: [ie.gemm(step.qp.view(S, H), w["wo"], step.ap, workspace=ws) for w in Ls],
+             2 * S * H * H),
+            ("gate_up_2x14336x4096", lambda: [ie.ffn_gate_up(step.xp, w["wg"], w["wu"], step.hp, workspace=ws)
+                                              for w in Ls], 2 * S * 2 * F * H),
+            ("down_4096x14336", lambda: [ie.gemm(step.hp, w["wd"], step.op, workspace=ws) for w in Ls], 2 * S * H * F),
+        )
+    for (name, fn, flops), (_, fn_whole, _) in zip(c3_cases(step.split_ws), c3_cases(None)):
         t = timed(fn, reps=2) / L
+        tw = timed(fn_whole, reps=2) / L
         c3[name] = {"us": round(t * 1e6, 1), "tflops": round(flops / t / 1e12, 1),
-                    "frac_burst": round(flops / t / 1e12 / tf_peak, 4)}
+                    "frac_burst": round(flops / t / 1e12 / tf_peak, 4), "whole_tiles_us": round(tw * 1e6, 1)}
     out["c3_prefill_m2048"] = c3
     return out
 
@@ -850,12 +861,18 @@ def parity_leg(torch, dev, seed, n_steps, batch=8):
     return out
 
 
-def tp_parity(torch, dist, dev, seed, rank, prompt, tp_ids, ctx):
-    """Rank 0 (untimed, after the timed steps): the single-GPU engine on the
-    full model from the same seeded generator, prefill of the same prompt and
-    as many greedy steps; its ids against the tensor-parallel engine's ids of
-    the run (prefill id, warm-up steps, timed steps). The other ranks wait."""
-    res = None
+def tp_parity(torch, dist, dev, seed, rank, prompt, tp_eng, tp_ids, ctx):
+    """Untimed, after the timed steps: rank 0 runs the single-GPU engine on
+    the full model from the same seeded generator (the same prompt, as many
+    greedy steps as the tensor-parallel run made) and broadcasts its ids.
+    Reported: the tensor-parallel run's own ids against them (free-running),
+    and a teacher-forced pass in which every rank's engine is fed the
+    single-GPU ids step by step, so that each step is scored on the same
+    context. The O and down partial sums meet in another order across ranks
+    than inside one GPU, so an id can flip where two logits tie to within a
+    rounding step."""
+    n = len(tp_ids)
+    ref = torch.zeros(n, dtype=torch.int32, device=dev)
     if rank == 0:
         layers, lm = make_weights(torch, dev, torch.bfloat16, seed)
         weights = full_model_weights(torch, dev, seed, layers, lm)
@@ -863,17 +880,24 @@ def tp_parity(torch, dist, dev, seed, rank, prompt, tp_ids, ctx):
         eng.prefill(0, prompt[:256])  # the same warm-up the TP run made
         eng.set_position(0, 0, 0)
         first = eng.prefill(0, prompt)
-        ids = np.concatenate([[first], eng.decode(len(tp_ids) - 1)[:, 0]]).astype(np.int32)
+        ids = np.concatenate([[first], eng.decode(n - 1)[:, 0]]).astype(np.int32)
         eng.close()
         del eng, weights, layers, lm
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
-        d = np.nonzero(ids != tp_ids)[0]
-        res = {"ids": len(tp_ids), "equal": int((ids == tp_ids).sum()), "identical": bool(len(d) == 0),
-               "first_difference": int(d[0]) if len(d) else None,
-               "against": "single-GPU engine, same seeded bf16 model and prompt"}
-    dist.barrier()
-    return res
+        ref.copy_(torch.from_numpy(ids))
+    dist.broadcast(ref, 0)
+    ref = ref.cpu().numpy()
+    tf = [int(tp_ids[0])]
+    for i in range(n - 1):  # every rank, in lockstep (the step holds collectives)
+        tp_eng.set_position(0, PROMPT + i, int(ref[i]))
+        tf.append(int(tp_eng.decode(1)[0, 0]))
+    tf = np.array(tf, np.int32)
+    d = np.nonzero(ref != tp_ids)[0]
+    return {"ids": n, "free_running_equal": int((ref == tp_ids).sum()), "identical": bool(len(d) == 0),
+            "free_running_first_difference": int(d[0]) if len(d) else None,
+            "teacher_forced_equal": int((tf == ref).sum()),
+            "against": "single-GPU engine, same seeded bf16 model and prompt"}
 
 
 # ------------------------------------------------------------------- main
@@ -1065,12 +1089,12 @@ def run_ours(torch, dist, dev, args, world, rank, local, hbm_peak, tf_peak, tf_p
     result["gpu_launches"] = (L * 7 + 4 + (1 if world > 1 else 0)) * args.steps
     result["prefill_engine"] = {"prompt": PROMPT, "ms": round(prefill_s * 1e3, 3),
                                 "tok_per_s": round(PROMPT / prefill_s, 1), "timing": "host wall clock, blocking call"}
+    if world > 1:
+        # the N-rank engine's ids of this run against the single-GPU engine's
+        result["tp_parity"] = tp_parity(torch, dist, dev, args.seed, rank, prompt, eng, run_ids, ctx)
     eng.close()
     del eng, es
     torch.cuda.synchronize()
-    if world > 1:
-        # the N-rank engine's ids of this run against the single-GPU engine's
-        result["tp_parity"] = tp_parity(torch, dist, dev, args.seed, rank, prompt, run_ids, ctx)
 
     # ---------------- the weight-matmul path alone (north-star target: >= 80 % of HBM)
     graph = torch.cuda.CUDAGraph()

@@ -162,6 +162,51 @@ int ie_qkv(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_di
            const float* rope_cos, const float* rope_sin,
            void* stream);
 
+/* ---- prefill projections with a split of the last wave ------------------
+ * ie_gemm, ie_gemm_add, ie_ffn_gate_up and ie_qkv with a caller-owned
+ * workspace. For M > 16 the tensor-core kernel runs one persistent CTA per
+ * SM; when the tiles leave SMs idle in the last wave it can run the full
+ * waves whole and split each tail tile's k-loop into up to 4 ranges spread
+ * over all SMs; the last range of a tile adds the others' fp32 partial sums,
+ * kept in the workspace, in range order and applies the fused epilogue. It
+ * does so for the plain projections (ie_gemm_ws, ie_gemm_add_ws) whose tiles
+ * fill less than one wave (short prefill chunks: at M = 128 the O projection
+ * takes 22 us instead of 30, down 41 instead of 91) or whose K is at least
+ * 8192 (down); ie_qkv_ws and ie_ffn_gate_up_ws accept the workspace but run
+ * whole tiles (measured: no gain). The split is chosen per shape and is
+ * deterministic; results may differ from the workspace-free call in their
+ * last bits (another fp32 summation order).
+ * workspace: ie_split_workspace_size() bytes (smaller ones allow fewer
+ * splits), 256-byte aligned, zero-filled once when allocated; every call that
+ * completes leaves its flag words zeroed again (after IE_ERR_TIMEOUT in
+ * ie_device_status, zero it again). NULL runs whole tiles. Calls sharing a
+ * workspace must not overlap on the GPU (one stream, or ordered streams).
+ * The split assumes that all SMs are available to the launch; with fewer, a
+ * tile's last range can wait until its bounded wait expires (IE_ERR_TIMEOUT).
+ * M <= 16 ignores the workspace. The reference has no counterpart (cuBLAS
+ * chooses its own split inside multiply_by_weight, kernels/ffn.cu:14). */
+size_t ie_split_workspace_size(void);
+int ie_gemm_ws(ie_dtype dt, int M, int N, int K,
+               const void* X, int64_t ldx,
+               const void* W, int64_t ldw,
+               void* Y, int64_t ldy,
+               void* workspace, size_t workspace_bytes, void* stream);
+int ie_gemm_add_ws(ie_dtype dt, int M, int N, int K,
+                   const void* X, int64_t ldx,
+                   const void* W, int64_t ldw,
+                   void* Y, int64_t ldy,
+                   void* workspace, size_t workspace_bytes, void* stream);
+int ie_ffn_gate_up_ws(ie_dtype dt, int M, int H, int F,
+                      const void* x, const void* W_gate, const void* W_up,
+                      void* h, int64_t ldh,
+                      void* workspace, size_t workspace_bytes, void* stream);
+int ie_qkv_ws(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_dim,
+              const void* x, const void* Wq, const void* Wk, const void* Wv,
+              void* q_out, void* k_cache, void* v_cache,
+              int64_t cache_head_stride, int pos0,
+              const float* rope_cos, const float* rope_sin,
+              void* workspace, size_t workspace_bytes, void* stream);
+
 /* Batched decode of B independent sequences (BASELINE config 5 at batch 8):
  * row b of x is a token of sequence b at position positions[b] (device array
  * [B]); its K/V rows go to sequence b's cache, which starts cache_batch_stride

@@ -59,7 +59,8 @@ EXPORTED_SYMBOLS = (
     "ie_attention_decode", "ie_gemm_add", "ie_gemm_allreduce_add", "ie_rmsnorm", "ie_embed", "ie_engine_create",
     "ie_engine_destroy", "ie_engine_prefill", "ie_engine_decode", "ie_engine_verify", "ie_engine_set_position",
     "ie_engine_position", "ie_engine_stream", "ie_engine_step", "ie_engine_create_tp", "ie_add_f32",
-    "ie_set_wait_limit_ns",
+    "ie_set_wait_limit_ns", "ie_split_workspace_size", "ie_gemm_ws", "ie_gemm_add_ws", "ie_ffn_gate_up_ws",
+    "ie_qkv_ws",
     "ie_st_open", "ie_st_close", "ie_st_count", "ie_st_name", "ie_st_info", "ie_llama_load", "ie_llama_model_desc",
     "ie_llama_model_shard", "ie_llama_model_free",
 )
@@ -89,6 +90,13 @@ def lib() -> ctypes.CDLL:
         L.ie_device_status.restype = i32
         L.ie_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]
         L.ie_set_wait_limit_ns.restype = i32
+        L.ie_split_workspace_size.restype = sz
+        L.ie_split_workspace_size.argtypes = []
+        L.ie_gemm_ws.argtypes = [i32, i32, i32, i32, vp, i64, vp, i64, vp, i64, vp, sz, vp]
+        L.ie_gemm_add_ws.argtypes = [i32, i32, i32, i32, vp, i64, vp, i64, vp, i64, vp, sz, vp]
+        L.ie_ffn_gate_up_ws.argtypes = [i32, i32, i32, i32, vp, vp, vp, vp, i64, vp, sz, vp]
+        L.ie_qkv_ws.argtypes = [i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, i64, i32, vp, vp, vp, sz,
+                                vp]
         L.ie_gemm.argtypes = [i32, i32, i32, i32, vp, i64, vp, i64, vp, i64, vp]
         L.ie_gemm_add.argtypes = [i32, i32, i32, i32, vp, i64, vp, i64, vp, i64, vp]
         L.ie_gemm_add.restype = i32
@@ -156,23 +164,49 @@ def _check(status: int, what: str) -> None:
 
 
 # -------------------------------------------------------------- C-ABI mirror
-def gemm_add(x, w, y, stream=None):
+def gemm_add(x, w, y, stream=None, workspace=None):
     """y[M,N] = round(y + round(x[M,K] . w[N,K]^T)) in place (ie_gemm_add):
-    a projection with the residual add fused."""
+    a projection with the residual add fused. workspace (split_workspace()):
+    ie_gemm_add_ws, the prefill kernel splits its last wave."""
     M, K = x.shape
     N = w.shape[0]
+    if workspace is not None:
+        _check(lib().ie_gemm_add_ws(_dt(x), M, N, K, _ptr(x), x.stride(0), _ptr(w), w.stride(0), _ptr(y),
+                                    y.stride(0), _ptr(workspace), _nbytes(workspace), _stream(stream)),
+               "ie_gemm_add_ws")
+        return
     _check(lib().ie_gemm_add(_dt(x), M, N, K, _ptr(x), x.stride(0), _ptr(w), w.stride(0), _ptr(y), y.stride(0),
                              _stream(stream)), "ie_gemm_add")
 
 
-def gemm(x, w, y, M=None, N=None, K=None, ldx=None, ldw=None, ldy=None, stream=None):
-    """y[M,N] = x[M,K] . w[N,K]^T (ie_gemm)."""
+def _nbytes(t) -> int:
+    return t.numel() * t.element_size()
+
+
+def split_workspace_bytes() -> int:
+    """ie_split_workspace_size: bytes of the prefill tail-split workspace."""
+    return int(lib().ie_split_workspace_size())
+
+
+def split_workspace(device="cuda"):
+    """A zeroed tail-split workspace for the *_ws entry points (256-byte
+    aligned, as torch's allocator returns)."""
+    import torch
+    return torch.zeros(split_workspace_bytes(), dtype=torch.uint8, device=device)
+
+
+def gemm(x, w, y, M=None, N=None, K=None, ldx=None, ldw=None, ldy=None, stream=None, workspace=None):
+    """y[M,N] = x[M,K] . w[N,K]^T (ie_gemm; ie_gemm_ws with a workspace)."""
     M = x.shape[0] if M is None else M
     K = x.shape[-1] if K is None else K
     N = w.shape[0] if N is None else N
     ldx = x.stride(0) if ldx is None else ldx
     ldw = w.stride(0) if ldw is None else ldw
     ldy = y.stride(0) if ldy is None else ldy
+    if workspace is not None:
+        _check(lib().ie_gemm_ws(_dt(x), M, N, K, _ptr(x), ldx, _ptr(w), ldw, _ptr(y), ldy, _ptr(workspace),
+                                _nbytes(workspace), _stream(stream)), "ie_gemm_ws")
+        return
     _check(lib().ie_gemm(_dt(x), M, N, K, _ptr(x), ldx, _ptr(w), ldw, _ptr(y), ldy, _stream(stream)), "ie_gemm")
 
 
@@ -183,10 +217,15 @@ def ffn_fused(x, w_up, w_down, w_gate, out, workspace, stream=None):
                         _ptr(workspace), workspace.numel() * workspace.element_size(), _stream(stream)), "ie_ffn")
 
 
-def ffn_gate_up(x, w_gate, w_up, h, stream=None):
-    """h = silu(x.Wg^T) * (x.Wu^T) with the reference's roundings (ie_ffn_gate_up)."""
+def ffn_gate_up(x, w_gate, w_up, h, stream=None, workspace=None):
+    """h = silu(x.Wg^T) * (x.Wu^T) with the reference's roundings
+    (ie_ffn_gate_up; ie_ffn_gate_up_ws with a workspace)."""
     M, H = x.shape
     F = w_gate.shape[0]
+    if workspace is not None:
+        _check(lib().ie_ffn_gate_up_ws(_dt(x), M, H, F, _ptr(x), _ptr(w_gate), _ptr(w_up), _ptr(h), h.stride(0),
+                                       _ptr(workspace), _nbytes(workspace), _stream(stream)), "ie_ffn_gate_up_ws")
+        return
     _check(lib().ie_ffn_gate_up(_dt(x), M, H, F, _ptr(x), _ptr(w_gate), _ptr(w_up), _ptr(h), h.stride(0),
                                 _stream(stream)), "ie_ffn_gate_up")
 
@@ -196,8 +235,13 @@ def ffn_workspace_bytes(M: int, F: int = FFN_DIM) -> int:
 
 
 def qkv(x, wq, wk, wv, q_out, k_cache, v_cache, cache_head_stride, pos0=0, rope_cos=None, rope_sin=None,
-        n_q_heads=NUM_Q_HEADS, n_kv_heads=NUM_KV_HEADS, head_dim=HEAD_DIM, stream=None):
+        n_q_heads=NUM_Q_HEADS, n_kv_heads=NUM_KV_HEADS, head_dim=HEAD_DIM, stream=None, workspace=None):
     M, H = x.shape
+    if workspace is not None:
+        _check(lib().ie_qkv_ws(_dt(x), M, H, n_q_heads, n_kv_heads, head_dim, _ptr(x), _ptr(wq), _ptr(wk), _ptr(wv),
+                               _ptr(q_out), _ptr(k_cache), _ptr(v_cache), cache_head_stride, pos0, _ptr(rope_cos),
+                               _ptr(rope_sin), _ptr(workspace), _nbytes(workspace), _stream(stream)), "ie_qkv_ws")
+        return
     _check(lib().ie_qkv(_dt(x), M, H, n_q_heads, n_kv_heads, head_dim, _ptr(x), _ptr(wq), _ptr(wk), _ptr(wv),
                         _ptr(q_out), _ptr(k_cache), _ptr(v_cache), cache_head_stride, pos0, _ptr(rope_cos),
                         _ptr(rope_sin), _stream(stream)), "ie_qkv")

@@ -74,7 +74,7 @@ int ie_set_wait_limit_ns(unsigned long long ns) {
 }
 
 static int gemm_store(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw,
-                      void* Y, int64_t ldy, bool residual, void* stream) {
+                      void* Y, int64_t ldy, bool residual, void* ws, size_t ws_bytes, void* stream) {
   if (!valid_dtype(dt) || M < 0 || N < 0 || K <= 0) return IE_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return IE_OK;
   if (K % 8) return IE_ERR_ALIGNMENT;
@@ -93,17 +93,30 @@ static int gemm_store(ie_dtype dt, int M, int N, int K, const void* X, int64_t l
   q.A = X; q.lda = ldx; q.B = W; q.ldb = ldw; q.M = M; q.N = N; q.K = K;
   q.D = Y; q.ldd = ldy; q.epi = TC_EPI_STORE;
   q.residual = residual;
+  if ((s = attach_split_workspace(q, ws, ws_bytes))) return s;
   return launch_tc_gemm(dt, q, as_stream(stream));
 }
 
 int ie_gemm(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, void* Y,
             int64_t ldy, void* stream) {
-  return gemm_store(dt, M, N, K, X, ldx, W, ldw, Y, ldy, false, stream);
+  return gemm_store(dt, M, N, K, X, ldx, W, ldw, Y, ldy, false, nullptr, 0, stream);
 }
 
 int ie_gemm_add(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, void* Y,
                 int64_t ldy, void* stream) {
-  return gemm_store(dt, M, N, K, X, ldx, W, ldw, Y, ldy, true, stream);
+  return gemm_store(dt, M, N, K, X, ldx, W, ldw, Y, ldy, true, nullptr, 0, stream);
+}
+
+size_t ie_split_workspace_size(void) { return split_workspace_bytes(); }
+
+int ie_gemm_ws(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, void* Y,
+               int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+  return gemm_store(dt, M, N, K, X, ldx, W, ldw, Y, ldy, false, workspace, workspace_bytes, stream);
+}
+
+int ie_gemm_add_ws(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, void* Y,
+                   int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+  return gemm_store(dt, M, N, K, X, ldx, W, ldw, Y, ldy, true, workspace, workspace_bytes, stream);
 }
 
 int ie_gemm_f32out(ie_dtype dt, int M, int N, int K, const void* X, int64_t ldx, const void* W, int64_t ldw, float* Y,
@@ -155,8 +168,8 @@ int ie_ffn(ie_dtype dt, int M, int H, int F, const void* x, const void* W_up, co
   return ie_gemm(dt, M, H, F, workspace, F, W_down, F, out, H, stream);
 }
 
-int ie_ffn_gate_up(ie_dtype dt, int M, int H, int F, const void* x, const void* W_gate, const void* W_up, void* h,
-                   int64_t ldh, void* stream) {
+static int ffn_gate_up(ie_dtype dt, int M, int H, int F, const void* x, const void* W_gate, const void* W_up,
+                       void* h, int64_t ldh, void* ws, size_t ws_bytes, void* stream) {
   if (!valid_dtype(dt) || M < 0 || H <= 0 || F <= 0) return IE_ERR_INVALID_ARG;
   if (M == 0) return IE_OK;
   if ((H % 8) || (F % 8)) return IE_ERR_ALIGNMENT;
@@ -174,7 +187,18 @@ int ie_ffn_gate_up(ie_dtype dt, int M, int H, int F, const void* x, const void* 
   TcGemmParams q;
   q.A = x; q.lda = H; q.B = W_gate; q.B2 = W_up; q.ldb = H; q.M = M; q.N = F; q.K = H;
   q.D = h; q.ldd = ldh; q.epi = TC_EPI_SWIGLU;
+  if ((s = attach_split_workspace(q, ws, ws_bytes))) return s;
   return launch_tc_gemm(dt, q, st);
+}
+
+int ie_ffn_gate_up(ie_dtype dt, int M, int H, int F, const void* x, const void* W_gate, const void* W_up, void* h,
+                   int64_t ldh, void* stream) {
+  return ffn_gate_up(dt, M, H, F, x, W_gate, W_up, h, ldh, nullptr, 0, stream);
+}
+
+int ie_ffn_gate_up_ws(ie_dtype dt, int M, int H, int F, const void* x, const void* W_gate, const void* W_up, void* h,
+                      int64_t ldh, void* workspace, size_t workspace_bytes, void* stream) {
+  return ffn_gate_up(dt, M, H, F, x, W_gate, W_up, h, ldh, workspace, workspace_bytes, stream);
 }
 
 namespace {
@@ -182,7 +206,7 @@ namespace {
 int qkv_common(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_dim, const void* x, const void* Wq,
                const void* Wk, const void* Wv, void* q_out, void* k_cache, void* v_cache, int64_t cache_head_stride,
                int pos0, const int* positions, int64_t cache_batch_stride, int cache_rows, const float* rope_cos,
-               const float* rope_sin, void* stream) {
+               const float* rope_sin, void* ws, size_t ws_bytes, void* stream) {
   if (!valid_dtype(dt) || M < 0 || H <= 0 || n_q_heads <= 0 || n_kv_heads < 0 || pos0 < 0) return IE_ERR_INVALID_ARG;
   if (head_dim != 128) return IE_ERR_UNSUPPORTED;
   if (M == 0) return IE_OK;
@@ -219,6 +243,7 @@ int qkv_common(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int hea
   q.k_cache = k_cache; q.v_cache = v_cache; q.cache_head_stride = cache_head_stride; q.pos0 = pos0;
   q.rope_cos = rope_cos; q.rope_sin = rope_sin;
   q.positions = positions; q.cache_batch_stride = cache_batch_stride; q.cache_rows = cache_rows;
+  if ((s = attach_split_workspace(q, ws, ws_bytes))) return s;
   return launch_tc_gemm(dt, q, st);
 }
 
@@ -228,7 +253,15 @@ int ie_qkv(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_di
            const void* Wk, const void* Wv, void* q_out, void* k_cache, void* v_cache, int64_t cache_head_stride,
            int pos0, const float* rope_cos, const float* rope_sin, void* stream) {
   return qkv_common(dt, M, H, n_q_heads, n_kv_heads, head_dim, x, Wq, Wk, Wv, q_out, k_cache, v_cache,
-                    cache_head_stride, pos0, nullptr, 0, 0, rope_cos, rope_sin, stream);
+                    cache_head_stride, pos0, nullptr, 0, 0, rope_cos, rope_sin, nullptr, 0, stream);
+}
+
+int ie_qkv_ws(ie_dtype dt, int M, int H, int n_q_heads, int n_kv_heads, int head_dim, const void* x, const void* Wq,
+              const void* Wk, const void* Wv, void* q_out, void* k_cache, void* v_cache, int64_t cache_head_stride,
+              int pos0, const float* rope_cos, const float* rope_sin, void* workspace, size_t workspace_bytes,
+              void* stream) {
+  return qkv_common(dt, M, H, n_q_heads, n_kv_heads, head_dim, x, Wq, Wk, Wv, q_out, k_cache, v_cache,
+                    cache_head_stride, pos0, nullptr, 0, 0, rope_cos, rope_sin, workspace, workspace_bytes, stream);
 }
 
 int ie_qkv_batched(ie_dtype dt, int B, int H, int n_q_heads, int n_kv_heads, int head_dim, const void* x,
@@ -237,7 +270,8 @@ int ie_qkv_batched(ie_dtype dt, int B, int H, int n_q_heads, int n_kv_heads, int
                    const float* rope_cos, const float* rope_sin, void* stream) {
   if (!positions || cache_rows <= 0) return IE_ERR_INVALID_ARG;
   return qkv_common(dt, B, H, n_q_heads, n_kv_heads, head_dim, x, Wq, Wk, Wv, q_out, k_cache, v_cache,
-                    cache_head_stride, 0, positions, cache_batch_stride, cache_rows, rope_cos, rope_sin, stream);
+                    cache_head_stride, 0, positions, cache_batch_stride, cache_rows, rope_cos, rope_sin, nullptr, 0,
+                    stream);
 }
 
 size_t ie_lm_head_argmax_workspace_size(int M) {

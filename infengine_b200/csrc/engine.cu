@@ -55,6 +55,9 @@ struct Engine {
       *ids = nullptr;
   void* lm_ws = nullptr;
   size_t lm_ws_bytes = 0;
+  // tail-split workspace of the prefill projections (chunks of > 16 rows)
+  void* split_ws = nullptr;
+  size_t split_ws_bytes = 0;
   std::vector<int> pos_host;
   long long step_host = 0;
   cudaGraph_t graph = nullptr;
@@ -92,7 +95,7 @@ int check(cudaError_t e) { return e == cudaSuccess ? IE_OK : IE_ERR_LAUNCH; }
 // NVLink exchange kernel (decode rows) or NCCL (longer chunks).
 int proj_add(Engine& E, int M, int K, const void* X, const void* W) {
   const int H = E.d.hidden;
-  if (E.world == 1) return ie_gemm_add(E.dt, M, H, K, X, K, W, K, E.x, H, E.st);
+  if (E.world == 1) return ie_gemm_add_ws(E.dt, M, H, K, X, K, W, K, E.x, H, E.split_ws, E.split_ws_bytes, E.st);
   if (E.has_ex && M <= 16 && M <= E.ex.max_rows)
     return ie_gemm_allreduce_add(E.dt, M, H, K, X, K, W, K, E.x, H, &E.ex, E.st);
   IE_TRY(ie_gemm_f32out(E.dt, M, H, K, X, K, W, K, E.part, H, E.st));
@@ -116,8 +119,8 @@ int layer_forward(Engine& E, int l, int M, int seq, int pos0) {
     IE_TRY(ie_attention_decode(E.dt, M, 1, nq, nkv, hd, E.q, (int64_t)M * hd, E.kcache(l, 0), E.vcache(l, 0), E.chs,
                                E.cbs, E.ctx, E.positions, 0, E.attn, (int64_t)nq * hd, st));
   } else {
-    IE_TRY(ie_qkv(E.dt, M, H, nq, nkv, hd, E.a, w.wq, w.wk, w.wv, E.q, E.kcache(l, seq), E.vcache(l, seq), E.chs,
-                  pos0, d.rope_cos, d.rope_sin, st));
+    IE_TRY(ie_qkv_ws(E.dt, M, H, nq, nkv, hd, E.a, w.wq, w.wk, w.wv, E.q, E.kcache(l, seq), E.vcache(l, seq), E.chs,
+                     pos0, d.rope_cos, d.rope_sin, E.split_ws, E.split_ws_bytes, st));
     if (M <= 16)
       IE_TRY(ie_attention_decode(E.dt, M, M, nq, nkv, hd, E.q, (int64_t)M * hd, E.kcache(l, seq), E.vcache(l, seq),
                                  E.chs, E.cbs, E.ctx, nullptr, pos0, E.attn, (int64_t)nq * hd, st));
@@ -127,7 +130,7 @@ int layer_forward(Engine& E, int l, int M, int seq, int pos0) {
   }
   IE_TRY(proj_add(E, M, nq * hd, E.attn, w.wo));
   IE_TRY(ie_rmsnorm(E.dt, M, H, E.x, H, w.ffn_norm, E.a, H, d.rms_eps, st));
-  IE_TRY(ie_ffn_gate_up(E.dt, M, H, F, E.a, w.w_gate, w.w_up, E.h, F, st));
+  IE_TRY(ie_ffn_gate_up_ws(E.dt, M, H, F, E.a, w.w_gate, w.w_up, E.h, F, E.split_ws, E.split_ws_bytes, st));
   IE_TRY(proj_add(E, M, F, E.h, w.w_down));
   return IE_OK;
 }
@@ -178,7 +181,7 @@ void release(Engine* E) {
   if (E->exec) cudaGraphExecDestroy(E->exec);
   if (E->graph) cudaGraphDestroy(E->graph);
   void* bufs[] = {E->x,       E->a,     E->q,    E->attn,  E->h,     E->kv,    E->tok_in, E->positions,
-                  E->history, E->step,  E->chunk, E->ids,  E->lm_ws, E->part, E->keys};
+                  E->history, E->step,  E->chunk, E->ids,  E->lm_ws, E->part, E->keys, E->split_ws};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (E->own_stream && E->st) cudaStreamDestroy(E->st);
@@ -272,6 +275,10 @@ int ie_engine_create_tp(ie_dtype dt, const ie_llama_desc* desc, int max_batch, i
   alloc(reinterpret_cast<void**>(&E->chunk), R * sizeof(int));
   alloc(reinterpret_cast<void**>(&E->ids), R * sizeof(int));
   alloc(&E->lm_ws, E->lm_ws_bytes);
+  if (E->max_rows > 16) {  // prefill chunks run the tensor-core kernels
+    E->split_ws_bytes = ie_split_workspace_size();
+    alloc(&E->split_ws, E->split_ws_bytes);
+  }
   if (E->world > 1) {
     alloc(reinterpret_cast<void**>(&E->part), R * H * sizeof(float));
     alloc(reinterpret_cast<void**>(&E->keys), (size_t)(max_batch > 16 ? max_batch : 16) * sizeof(unsigned long long));
@@ -282,6 +289,7 @@ int ie_engine_create_tp(ie_dtype dt, const ie_llama_desc* desc, int max_batch, i
          cudaMemsetAsync(E->positions, 0, max_batch * sizeof(int), E->st) == cudaSuccess &&
          cudaMemsetAsync(E->step, 0, sizeof(int), E->st) == cudaSuccess &&
          cudaMemsetAsync(E->lm_ws, 0, E->lm_ws_bytes, E->st) == cudaSuccess &&
+         (!E->split_ws || cudaMemsetAsync(E->split_ws, 0, E->split_ws_bytes, E->st) == cudaSuccess) &&
          cudaStreamSynchronize(E->st) == cudaSuccess;
   }
   if (!ok) {

@@ -25,6 +25,24 @@
 //   ARGMAX — 256 consecutive vocabulary rows.
 // No TMA multicast and no clusters: every load reads this GPU's own memory.
 //
+// Tail split (a separate instantiation, SPLIT = true, used when the caller
+// passes a workspace). With W tiles on G persistent CTAs the last wave holds
+// R = W mod G tiles and leaves G - R SMs idle (O and down at M = 2048: 256
+// tiles, 108 in the second wave of 148). The SPLIT kernel runs the first
+// W - R tiles whole, exactly as above, then splits each of the R tail tiles
+// into s ranges of k-blocks, numbered split-major (unit j * R + r is range j
+// of tail tile r), so that in every round all CTAs stream the same k-slices
+// of the operands (L2 sharing stays as in the whole-tile waves). Ranges
+// 0 .. s-2 store their fp32 partial tile in the workspace and count it on a
+// per-(tile, warp quarter) flag; range s-1 waits (bounded) for its flag,
+// adds the partials in range order, then its own accumulator, and runs the
+// fused epilogue on the sum. A unit only waits for units with a lower index,
+// which no CTA reaches after a higher one, so the waits cannot form a cycle.
+// The summation order is fixed: results are deterministic (their last bits
+// differ from the whole-tile kernel's). The host picks s per shape from a
+// wave count plus the fix-up reads (plan_split), for the shapes where the
+// split measured faster (see launch_tc_gemm).
+//
 // Every mbarrier wait is bounded by the global timer; a wait that gives up
 // records IE_ERR_TIMEOUT in a device status word (ie_device_status()), makes
 // every role leave its loop, drains the copies and MMAs the CTA issued and
@@ -32,6 +50,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include "ie_common.cuh"
@@ -53,6 +72,7 @@ constexpr int STAGE_BYTES = A_TILE + 2 * B_HALF;
 constexpr int TILE_BYTES = STAGES * STAGE_BYTES;  // 192 KB
 constexpr int SMEM_BYTES = TILE_BYTES + 1024 + 256;
 constexpr int THREADS = 192;
+constexpr int kMaxSplit = 4;  // k-ranges per split tile (the fix-up holds s - 1 partial chunks)
 constexpr uint32_t TMEM_COLS = 512;
 
 struct TcArgs {
@@ -61,7 +81,40 @@ struct TcArgs {
   TcGemmParams p;
   int nm, nn, nk;
   int heads;  // QKV: n_q_heads + 2 * n_kv_heads
+  // tail split (SPLIT kernel): whole tiles [0, split_F * gridDim.x), then
+  // split_R tiles in split_s k-ranges each
+  int split_s, split_F, split_R;
 };
+
+// One unit of a CTA's work: tile `tile`, k-blocks [k0, k1); j = -1 for a
+// whole tile, else k-range j of tail tile r.
+struct Unit {
+  int tile, k0, k1, j, r;
+};
+// The q-th unit of this CTA (false when it has no more).
+template <bool SPLIT>
+__device__ __forceinline__ bool unit_at(const TcArgs& a, int q, Unit& u) {
+  const int v = (int)blockIdx.x + q * (int)gridDim.x;
+  if constexpr (!SPLIT) {
+    if (v >= a.nm * a.nn) return false;
+    u.tile = v; u.k0 = 0; u.k1 = a.nk; u.j = -1; u.r = 0;
+    return true;
+  } else {
+    const int whole = a.split_F * (int)gridDim.x;
+    if (v < whole) {
+      u.tile = v; u.k0 = 0; u.k1 = a.nk; u.j = -1; u.r = 0;
+      return true;
+    }
+    const int w = v - whole;
+    if (w >= a.split_R * a.split_s) return false;
+    u.j = w / a.split_R;
+    u.r = w - u.j * a.split_R;
+    u.tile = whole + u.r;
+    u.k0 = u.j * a.nk / a.split_s;
+    u.k1 = (u.j + 1) * a.nk / a.split_s;
+    return true;
+  }
+}
 
 // ------------------------------------------------------------ PTX helpers
 using namespace tc;
@@ -71,6 +124,52 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 template <typename T>
 __device__ __forceinline__ uint32_t idesc_f16() {
   return tc::idesc_f16<T>(BM, BN);
+}
+// Lane 0 waits (bounded) until *f reaches target, with acquire ordering at
+// GPU scope; the warp then continues together. False on timeout or abort.
+__device__ __forceinline__ bool wait_count(const unsigned int* f, unsigned int target, volatile int* abort_flag,
+                                           int lane) {
+  int ok = 1;
+  if (lane == 0) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    if (v < target) {
+      const unsigned long long limit = g_tc_wait_ns;
+      const unsigned long long t0 = globaltimer();
+      while (true) {
+        if (*abort_flag) { ok = 0; break; }
+        __nanosleep(64);
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        if (v >= target) break;
+        if (globaltimer() - t0 > limit) {
+          atomicExch(&g_tc_status, IE_ERR_TIMEOUT);
+          *abort_flag = 1;
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+// Partial tile in the workspace (128 x 256 fp32 = 128 KB), laid out as
+// [32-column chunk c][float4 group i of the chunk][row][4]: the 32 rows of an
+// epilogue warp then read or write 512 contiguous bytes per access. Accessed
+// through L2 only (other SMs write and read it).
+__device__ __forceinline__ void store32_part(float* slot, int row, int c, const float (&v)[32]) {
+  float4* q = reinterpret_cast<float4*>(slot) + (size_t)c * 8 * BM + row;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) __stcg(q + i * BM, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+}
+__device__ __forceinline__ void load32_part(const float* slot, int row, int c, float (&v)[32]) {
+  const float4* q = reinterpret_cast<const float4*>(slot) + (size_t)c * 8 * BM + row;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 x = __ldcg(q + i * BM);
+    v[4 * i] = x.x; v[4 * i + 1] = x.y; v[4 * i + 2] = x.z; v[4 * i + 3] = x.w;
+  }
 }
 
 // Store 32 consecutive values of one output row (columns col0.. col0+31,
@@ -129,7 +228,7 @@ __device__ __forceinline__ void b_source(const TcArgs& a, int nb, int h, int& ma
   }
 }
 
-template <typename T, int EPI>
+template <typename T, int EPI, bool SPLIT>
 __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -143,6 +242,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const TcGemmParams& p = args.p;
   const int num_tiles = args.nm * args.nn;
+  (void)num_tiles;
 
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
   auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
@@ -187,9 +287,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
       // ------------------------------------------------ TMA producer
       int stage = 0, issued = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        const int mb = tile % args.nm, nb = tile / args.nm;
-        for (int kb = 0; kb < args.nk; ++kb) {
+      Unit u;
+      for (int q = 0; !*abort_flag && unit_at<SPLIT>(args, q, u); ++q) {
+        const int mb = u.tile % args.nm, nb = u.tile / args.nm;
+        for (int kb = u.k0; kb < u.k1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag)) break;
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
           mbar_expect_tx(full_bar(stage), STAGE_BYTES);
@@ -214,19 +315,20 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
       int stage = 0, consumed = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool issued_any = false;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+      Unit u;
+      for (int q = 0; !*abort_flag && unit_at<SPLIT>(args, q, u); ++q) {
         if (!mbar_wait(acce_bar(acc), acc_phase ^ 1, abort_flag)) break;
         fence_after();
         const uint32_t d_tmem = tmem + acc * BN;
         bool ok = true;
-        for (int kb = 0; kb < args.nk; ++kb) {
+        for (int kb = u.k0; kb < u.k1; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
           fence_after();
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
           const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sa + A_TILE);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            mma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            mma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb != u.k0 || k != 0) ? 1u : 0u);
           mma_commit(empty_bar(stage));
           issued_any = true;
           ++consumed;
@@ -252,38 +354,89 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
     const int row = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-      const int mb = tile % args.nm, nb = tile / args.nm;
+    Unit u;
+    for (int q = 0; !*abort_flag && unit_at<SPLIT>(args, q, u); ++q) {
+      const int mb = u.tile % args.nm, nb = u.tile / args.nm;
       if (!mbar_wait(accf_bar(acc), acc_phase, abort_flag)) break;
       fence_after();
       const uint32_t tbase = tmem + acc * BN + ((uint32_t)(quad * 32) << 16);
       const int m = mb * BM + row;
       const bool mvalid = m < p.M;
       float v[32];
-      if constexpr (EPI == TC_EPI_STORE_F32) {
-        float* drow = static_cast<float*>(p.D) + (int64_t)m * p.ldd;
+      // tail split: ranges 0 .. s-2 hand their partial sums to range s-1
+      bool producer = false;
+      const float* parts = nullptr;  // range s-1: the tile's first partial
+      unsigned int* flag = nullptr;
+      if constexpr (SPLIT) {
+        if (u.j >= 0) {
+          flag = p.split_flags + u.r * 4 + quad;
+          if (u.j < args.split_s - 1) {
+            producer = true;
+          } else {
+            if (!wait_count(flag, (unsigned)(args.split_s - 1), abort_flag, lane)) break;
+            parts = p.split_ws + (size_t)u.r * (args.split_s - 1) * BM * BN;
+          }
+        }
+      }
+      // 32 accumulator columns from col: with partials, sum = p_0 + ... +
+      // p_{s-2} + own, in that order
+      auto acc_ld = [&](int col, float (&x)[32]) {
+        tmem_ld32(tbase + col, x);
+        if constexpr (SPLIT) {
+          if (parts) {
+            // all partials of the chunk requested together (s <= kMaxSplit),
+            // then added in range order
+            const int np = args.split_s - 1;
+            float p0[32], p1[32], p2[32];
+            load32_part(parts, row, col >> 5, p0);
+            if (np > 1) load32_part(parts + (size_t)BM * BN, row, col >> 5, p1);
+            if (np > 2) load32_part(parts + (size_t)2 * BM * BN, row, col >> 5, p2);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              float sum = p0[i];
+              if (np > 1) sum += p1[i];
+              if (np > 2) sum += p2[i];
+              x[i] = sum + x[i];
+            }
+          }
+        }
+      };
+      if (producer) {
+        float* slot = p.split_ws + (size_t)(u.r * (args.split_s - 1) + u.j) * BM * BN;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           tmem_ld32(tbase + c * 32, v);
+          store32_part(slot, row, c, v);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          __threadfence();
+          atomicAdd(flag, 1u);
+        }
+      } else if constexpr (EPI == TC_EPI_STORE_F32) {
+        float* drow = static_cast<float*>(p.D) + (int64_t)m * p.ldd;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          acc_ld(c * 32, v);
           if (mvalid) store_row32_f32(drow, nb * BN + c * 32, p.N, v);
         }
       } else if constexpr (EPI == TC_EPI_STORE) {
         T* drow = static_cast<T*>(p.D) + (int64_t)m * p.ldd;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
-          tmem_ld32(tbase + c * 32, v);
+          acc_ld(c * 32, v);
           if (mvalid) store_row32<T>(drow, nb * BN + c * 32, p.N, v, p.residual);
         }
       } else if constexpr (EPI == TC_EPI_SWIGLU) {
         T* drow = static_cast<T*>(p.D) + (int64_t)m * p.ldd;
-        float u[32];
+        float uu[32];
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-          tmem_ld32(tbase + c * 32, v);
-          tmem_ld32(tbase + 128 + c * 32, u);
+          acc_ld(c * 32, v);
+          acc_ld(128 + c * 32, uu);
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const float gv = round_to<T>(v[i]), uv = round_to<T>(u[i]);
+            const float gv = round_to<T>(v[i]), uv = round_to<T>(uu[i]);
             v[i] = gv * (1.0f / (1.0f + expf(-gv))) * uv;
           }
           if (mvalid) store_row32<T>(drow, nb * 128 + c * 32, p.N, v);
@@ -321,8 +474,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
           }
 #pragma unroll 1
           for (int c = 0; c < 2; ++c) {
-            tmem_ld32(tbase + h * 128 + c * 32, v);       // d in [32c, 32c+32)
-            tmem_ld32(tbase + h * 128 + 64 + c * 32, b);  // d + 64
+            acc_ld(h * 128 + c * 32, v);       // d in [32c, 32c+32)
+            acc_ld(h * 128 + 64 + c * 32, b);  // d + 64
             // this row's 32 table entries, as 16-byte vectors (tables are
             // 16-byte aligned and rows are 256 bytes)
             float cs[32], sn[32];
@@ -359,7 +512,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
         unsigned long long best = 0ull;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
-          tmem_ld32(tbase + c * 32, v);
+          acc_ld(c * 32, v);
           const int col0 = nb * BN + c * 32;
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
@@ -373,13 +526,19 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
         }
         if (mvalid && best) atomicMax(p.keys + m, best);
       }
+      if constexpr (SPLIT) {
+        if (parts) {  // partials read: lower the flag for the next call
+          __syncwarp();
+          if (lane == 0) *flag = 0u;
+        }
+      }
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_bar(acc));
       if constexpr (EPI == TC_EPI_ARGMAX) {
         // each epilogue warp counts its own part of the tile after its
         // atomics; the warp that brings the count to 4 * tiles finalizes
-        if (lane == 0) {
+        if (lane == 0 && !producer) {
           __threadfence();
           if (atomicAdd(p.counter, 1u) == 4u * (unsigned)num_tiles - 1u) {
             __threadfence();
@@ -441,10 +600,10 @@ int sm_count() {
   return n;
 }
 
-template <typename T, int EPI>
+template <typename T, int EPI, bool SPLIT>
 int launch_t(TcArgs& a, cudaStream_t st) {
   static bool configured = false;
-  auto kernel = tc_gemm_kernel<T, EPI>;
+  auto kernel = tc_gemm_kernel<T, EPI, SPLIT>;
   if (!configured) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
       return IE_ERR_LAUNCH;
@@ -452,7 +611,8 @@ int launch_t(TcArgs& a, cudaStream_t st) {
   }
   const int tiles = a.nm * a.nn;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(tiles < sm_count() ? tiles : sm_count());
+  // the split plan assumes one persistent CTA per SM
+  cfg.gridDim = dim3(SPLIT ? sm_count() : (tiles < sm_count() ? tiles : sm_count()));
   cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = st;
@@ -469,16 +629,59 @@ int launch_t(TcArgs& a, cudaStream_t st) {
   return IE_OK;
 }
 
-template <typename T>
+template <typename T, bool SPLIT>
 int dispatch(TcArgs& a, int epi, cudaStream_t st) {
   switch (epi) {
-    case TC_EPI_STORE: return launch_t<T, TC_EPI_STORE>(a, st);
-    case TC_EPI_SWIGLU: return launch_t<T, TC_EPI_SWIGLU>(a, st);
-    case TC_EPI_QKV: return launch_t<T, TC_EPI_QKV>(a, st);
-    case TC_EPI_ARGMAX: return launch_t<T, TC_EPI_ARGMAX>(a, st);
-    case TC_EPI_STORE_F32: return launch_t<T, TC_EPI_STORE_F32>(a, st);
+    case TC_EPI_STORE: return launch_t<T, TC_EPI_STORE, SPLIT>(a, st);
+    case TC_EPI_SWIGLU: return launch_t<T, TC_EPI_SWIGLU, SPLIT>(a, st);
+    case TC_EPI_QKV: return launch_t<T, TC_EPI_QKV, SPLIT>(a, st);
+    case TC_EPI_ARGMAX: return launch_t<T, TC_EPI_ARGMAX, SPLIT>(a, st);
+    case TC_EPI_STORE_F32: return launch_t<T, TC_EPI_STORE_F32, SPLIT>(a, st);
   }
   return IE_ERR_UNSUPPORTED;
+}
+
+// Split of the last wave's tiles (SPLIT kernel): s k-ranges for each of the
+// R = W mod G tail tiles, or s = 1 (whole-tile kernel). In tile-times of
+// the tail, whole tiles cost 1; s ranges in ceil(R s / G) rounds cost
+// rounds / s, plus the hand-off at the end of the kernel: the partial stores
+// and the last range's chunk-by-chunk reads of the others' partials, each
+// chunk one L2 round trip (~3-4 us in all on B200, against ~0.43 us of MMAs
+// per k-block, hence 8 / nk tile-times). Ranges keep at least 4 k-blocks so
+// the 4-stage ring fills; the workspace bounds R (s - 1). IE_TC_SPLIT_MAX in
+// the environment lowers the largest s (1 turns the split off).
+int split_max() {
+  static const int v = [] {
+    const char* e = getenv("IE_TC_SPLIT_MAX");
+    const int x = e ? atoi(e) : kMaxSplit;
+    return x < 1 ? 1 : (x > kMaxSplit ? kMaxSplit : x);
+  }();
+  return v;
+}
+struct SplitPlan {
+  int s = 1, F = 0, R = 0;
+};
+SplitPlan plan_split(int tiles, int nk, int G, long long slots_cap) {
+  SplitPlan best;
+  if (tiles <= 0 || G <= 0) return best;
+  const int F = tiles / G, R = tiles - F * G;
+  if (R == 0) return best;
+  double best_cost = 1.0;
+  for (int s = 2; s <= split_max(); ++s) {
+    if (nk / s < 4) break;
+    if ((long long)R * (s - 1) > slots_cap) break;
+    const int rounds = (R * s + G - 1) / G;
+    const double cost = (double)rounds / s + 8.0 / nk;
+    if (cost < best_cost - 0.02) {
+      best_cost = cost;
+      best.s = s;
+    }
+  }
+  if (best.s > 1) {
+    best.F = F;
+    best.R = R;
+  }
+  return best;
 }
 
 }  // namespace
@@ -518,7 +721,41 @@ int launch_tc_gemm(ie_dtype dt, const TcGemmParams& p, cudaStream_t st) {
     default:
       return IE_ERR_UNSUPPORTED;
   }
-  return dt == IE_DTYPE_BF16 ? dispatch<__nv_bfloat16>(a, p.epi, st) : dispatch<__half>(a, p.epi, st);
+  a.split_s = 1;
+  // Where the split pays, measured on B200 (per-layer times over 32 layers'
+  // weights): plain-store GEMMs whose tiles fill less than one wave (M = 128:
+  // O 29.6 -> 22.2 us, down 91.1 -> 40.7 us) or whose K is long enough to
+  // amortise the hand-off (down at M = 2048: about -5 %). It did not pay for
+  // the QKV and SwiGLU epilogues (QKV at M = 2048: 91 -> 98 us) nor for
+  // K = 4096 over more than one wave (O at M = 2048: 55 -> 68 us).
+  const bool split_shape = p.epi != TC_EPI_QKV && p.epi != TC_EPI_SWIGLU &&
+                           (a.nm * a.nn < sm_count() || a.nk >= 128);
+  if (split_shape && p.split_ws && p.split_flags && p.split_slots > 0) {
+    const SplitPlan sp = plan_split(a.nm * a.nn, a.nk, sm_count(), p.split_slots);
+    a.split_s = sp.s;
+    a.split_F = sp.F;
+    a.split_R = sp.R;
+  }
+  if (a.split_s > 1)
+    return dt == IE_DTYPE_BF16 ? dispatch<__nv_bfloat16, true>(a, p.epi, st) : dispatch<__half, true>(a, p.epi, st);
+  return dt == IE_DTYPE_BF16 ? dispatch<__nv_bfloat16, false>(a, p.epi, st) : dispatch<__half, false>(a, p.epi, st);
+}
+
+// Workspace of the tail split: per-(tile, warp quarter) flags for up to one
+// wave of tail tiles, then the partial tiles (128 x 256 fp32 each), room for
+// three waves of them.
+size_t split_flags_bytes() { return ((size_t)sm_count() * 4 * sizeof(unsigned int) + 255) / 256 * 256; }
+size_t split_workspace_bytes() { return split_flags_bytes() + (size_t)3 * sm_count() * BM * BN * sizeof(float); }
+
+int attach_split_workspace(TcGemmParams& q, void* ws, size_t bytes) {
+  if (!ws) return IE_OK;  // no workspace: whole tiles
+  if (reinterpret_cast<uintptr_t>(ws) & 255u) return IE_ERR_ALIGNMENT;
+  const size_t fb = split_flags_bytes();
+  if (bytes < fb + (size_t)BM * BN * sizeof(float)) return IE_ERR_WORKSPACE;
+  q.split_flags = static_cast<unsigned int*>(ws);
+  q.split_ws = reinterpret_cast<float*>(static_cast<char*>(ws) + fb);
+  q.split_slots = (long long)((bytes - fb) / ((size_t)BM * BN * sizeof(float)));
+  return IE_OK;
 }
 
 cudaError_t set_tc_wait_ns(unsigned long long ns) {

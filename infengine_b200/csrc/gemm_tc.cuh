@@ -48,10 +48,21 @@ struct TcGemmParams {
   const int* positions = nullptr;
   int64_t cache_batch_stride = 0;
   int cache_rows = 0;
+  // split of the last wave's tiles along k (caller workspace, see
+  // attach_split_workspace); null: whole tiles only
+  unsigned int* split_flags = nullptr;
+  float* split_ws = nullptr;
+  long long split_slots = 0;  // partial tiles the workspace holds
 };
 
 // Returns an IE_* status.
 int launch_tc_gemm(ie_dtype dt, const TcGemmParams& p, cudaStream_t st);
+
+// Bytes of a tail-split workspace for this device (ie_split_workspace_size).
+size_t split_workspace_bytes();
+// Points q at a caller workspace (256-byte aligned; its flag words zeroed
+// once when allocated). ws == NULL leaves q on whole tiles.
+int attach_split_workspace(TcGemmParams& q, void* ws, size_t bytes);
 
 // Device status word written by timed-out waits (IE_OK or IE_ERR_TIMEOUT).
 int read_tc_status(bool clear);

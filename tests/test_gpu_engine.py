@@ -21,8 +21,15 @@ from conftest import from_dev, oracle, to_dev
 pytestmark = pytest.mark.gpu
 
 REF = Path(__file__).resolve().parent.parent / "oracle" / "_ref"
-N_PROMPT, N_NEW, SEED = 64, 24, 1234
-MARGIN_NOISE = 0.05
+N_PROMPT, N_NEW, SEED = 2048, 64, 1234
+# A greedy id may differ from the reference's only at a near-tie: the
+# reference's top-2 logit margin at most NEAR_TIE_ULPS fp16 spacings of its
+# top logit. cuBLAS (the reference's matmul) sums in an order of its own, so
+# the hidden states of the two runs differ in their last bits after 32
+# layers; measured over 2048 teacher-forced steps (8 prompts x 256), every
+# miss sat at <= 5 spacings and 7 of 35 were exact ties.
+NEAR_TIE_ULPS = 8
+MIN_AGREEMENT = 0.9  # a guard against wholesale failure; the near-tie bar is the contract
 LLAMA = dict(n_layers=32, hidden=4096, n_q_heads=32, n_kv_heads=8, head_dim=128, ffn_dim=14336, vocab=128256,
              rms_eps=1e-5)
 
@@ -96,7 +103,14 @@ def _load_model(name):
     L.model_generate.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                                  ctypes.c_void_p]
     L.model_weight_ptrs.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    L.model_generate_ex.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     return L
+
+
+def fp16_spacing(x):
+    """Spacing of fp16 numbers at |x|."""
+    return 2.0 ** (np.floor(np.log2(np.maximum(np.abs(x), 2.0 ** -14))) - 10)
 
 
 def _weights_from(L):
@@ -118,8 +132,10 @@ def test_engine_matches_reference_decode_loop(ie, cuda):
     try:
         toks_ref = np.zeros(N_NEW, np.int32)
         m_ref = np.zeros(N_NEW, np.float32)
-        assert L.model_generate(prompt.ctypes.data_as(ctypes.c_void_p), N_PROMPT, N_NEW, None,
-                                toks_ref.ctypes.data_as(ctypes.c_void_p), m_ref.ctypes.data_as(ctypes.c_void_p)) == 0
+        top_ref = np.zeros(N_NEW, np.float32)
+        vp = ctypes.c_void_p
+        assert L.model_generate_ex(prompt.ctypes.data_as(vp), N_PROMPT, N_NEW, None, toks_ref.ctypes.data_as(vp),
+                                   m_ref.ctypes.data_as(vp), top_ref.ctypes.data_as(vp), None, None) == 0
         eng = LlamaEngine(_weights_from(L), LLAMA, dtype="f16", max_batch=1, max_ctx=N_PROMPT + N_NEW + 8,
                           max_prefill=N_PROMPT)
         try:
@@ -140,11 +156,13 @@ def test_engine_matches_reference_decode_loop(ie, cuda):
     finally:
         L.model_free()
     agree = tf == toks_ref
+    ulps = m_ref / fp16_spacing(top_ref)
     first_div = int(np.argmin(free == toks_ref)) if not np.all(free == toks_ref) else N_NEW
-    print(f"engine vs reference loop: teacher-forced {agree.sum()}/{N_NEW}; free-running identical for "
-          f"{first_div} steps; reference margins at disagreements {m_ref[~agree].tolist()}")
-    assert agree.mean() >= 0.9
-    assert np.all(m_ref[~agree] < MARGIN_NOISE), (toks_ref, tf, m_ref)
+    print(f"engine vs reference loop ({N_PROMPT}-token prompt): teacher-forced {agree.sum()}/{N_NEW}; "
+          f"free-running identical for {first_div} steps; reference margins at disagreements, in fp16 spacings "
+          f"of the top logit: {ulps[~agree].tolist()}")
+    assert np.all(ulps[~agree] <= NEAR_TIE_ULPS), (toks_ref, tf, m_ref, top_ref)
+    assert agree.mean() >= MIN_AGREEMENT
     assert np.array_equal(ver, free[1:6]), (ver, free)
 
 

@@ -2,7 +2,10 @@
 
 Every call goes through the C-ABI. The bar is the same as for the decode
 kernels: each output within one rounding step of the exact sum, per-GEMM max
-relative error <= 1e-2 against the fp32 golden, argmax ids bit-exact.
+relative error <= 1e-2 against the fp32 golden, argmax ids bit-exact. The
+projections are checked twice: whole tiles (ie_gemm, ie_qkv, ...) and with
+the tail split of the *_ws entry points, which must also be deterministic
+and leave its workspace flags zeroed.
 """
 import numpy as np
 import pytest
@@ -30,11 +33,53 @@ def _device_status_clean(ie, cuda):
 ])
 def test_gemm_tensor_core(ie, cuda, dt, M, N, K):
     d = oracle.seeded_inputs(M + 7 * N + K, {"x": (M, K), "w": (N, K)}, dt)
-    y = cuda.full((M, N), float("nan"), dtype=torch_dtype(dt), device="cuda")
-    ie.gemm(to_dev(d["x"], dt), to_dev(d["w"], dt), y)
-    got = from_dev(y)
-    assert not np.isnan(got).any()
-    assert_within_one_rounding(got, oracle.gemm_fp32(d["x"], d["w"]), dt)
+    gold = oracle.gemm_fp32(d["x"], d["w"])
+    x, w = to_dev(d["x"], dt), to_dev(d["w"], dt)
+    ws = ie.split_workspace()
+    for workspace in (None, ws):
+        y = cuda.full((M, N), float("nan"), dtype=torch_dtype(dt), device="cuda")
+        ie.gemm(x, w, y, workspace=workspace)
+        got = from_dev(y)
+        assert not np.isnan(got).any()
+        assert_within_one_rounding(got, gold, dt)
+    assert_split_workspace_clean(ie, cuda, ws)
+
+
+def assert_split_workspace_clean(ie, cuda, ws):
+    """Every completed call leaves the split workspace's flag words zeroed."""
+    cuda.cuda.synchronize()
+    n = (cuda.cuda.get_device_properties(0).multi_processor_count * 16 + 255) // 256 * 256
+    assert int(ws[:n].count_nonzero().item()) == 0
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("M,N,K", [
+    (2048, 4096, 4096),   # O: 256 tiles on 148 SMs, 108 of them split
+    (2048, 6144, 4096),   # QKV-sized plain GEMM: 384 tiles
+    (256, 4096, 4096),    # 32 tiles, every one split
+    (40, 4096, 14336),    # an engine prefill chunk through the down projection
+    (300, 1000, 520),     # ragged: partial tiles in M, N and K
+])
+def test_gemm_tail_split_deterministic_and_residual(ie, cuda, dt, M, N, K):
+    """The tail split is deterministic (repeated calls give the same bits),
+    stays within one rounding step of the exact sum, and its residual form
+    equals round(y + round(split result)) exactly."""
+    d = oracle.seeded_inputs(5 * M + N + K, {"x": (M, K), "w": (N, K), "r": (M, N)}, dt)
+    x, w = to_dev(d["x"], dt), to_dev(d["w"], dt)
+    ws = ie.split_workspace()
+    T = torch_dtype(dt)
+    y1, y2 = (cuda.empty((M, N), dtype=T, device="cuda") for _ in range(2))
+    ie.gemm(x, w, y1, workspace=ws)
+    ie.gemm(x, w, y2, workspace=ws)
+    cuda.cuda.synchronize()
+    assert cuda.equal(y1, y2)
+    assert_within_one_rounding(from_dev(y1), oracle.gemm_fp32(d["x"], d["w"]), dt)
+    res = to_dev(d["r"], dt)
+    y3 = res.clone()
+    ie.gemm_add(x, w, y3, workspace=ws)
+    cuda.cuda.synchronize()
+    assert cuda.equal(y3, (res.float() + y1.float()).to(T))
+    assert_split_workspace_clean(ie, cuda, ws)
 
 
 def test_gemm_tensor_core_strided_output(ie, cuda):
@@ -54,16 +99,20 @@ def test_ffn_gate_up_swiglu_tensor_core(ie, cuda, dt, M):
     M=128 is the shape of the reference's own test_ffn.cu)."""
     H, F = 4096, 14336
     d = oracle.seeded_inputs(60 + M, {"x": (M, H), "wg": (F, H), "wu": (F, H)}, dt)
-    h = cuda.empty((M, F), dtype=torch_dtype(dt), device="cuda")
-    ie.ffn_gate_up(to_dev(d["x"], dt), to_dev(d["wg"], dt), to_dev(d["wu"], dt), h)
-    got = from_dev(h)
     g = oracle.gemm_fp32(d["x"], d["wg"])
     u = oracle.gemm_fp32(d["x"], d["wu"])
     want = oracle.swiglu(oracle.round_dt(g, dt), oracle.round_dt(u, dt), dt)
-    # g/u may round one step differently from the oracle's exact sums
-    close = np.abs(got - want) <= 2 * ulp(want, dt) + 1e-5 * np.abs(want).max()
-    assert close.mean() > 0.999
-    assert oracle.normwise_rel_err(got, want) < 2e-3
+    x, wg, wu = to_dev(d["x"], dt), to_dev(d["wg"], dt), to_dev(d["wu"], dt)
+    ws = ie.split_workspace()
+    for workspace in (None, ws):  # whole tiles, then the tail split
+        h = cuda.empty((M, F), dtype=torch_dtype(dt), device="cuda")
+        ie.ffn_gate_up(x, wg, wu, h, workspace=workspace)
+        got = from_dev(h)
+        # g/u may round one step differently from the oracle's exact sums
+        close = np.abs(got - want) <= 2 * ulp(want, dt) + 1e-5 * np.abs(want).max()
+        assert close.mean() > 0.999
+        assert oracle.normwise_rel_err(got, want) < 2e-3
+    assert_split_workspace_clean(ie, cuda, ws)
 
 
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
@@ -92,21 +141,25 @@ def test_qkv_tensor_core(ie, cuda, dt, M, pos0, nq, nkv):
                                            "wv": (nkv * hd, H)}, dt)
     cos, sin = oracle.rope_tables(ctx)
     T = torch_dtype(dt)
-    q = cuda.empty((nq, M, hd), dtype=T, device="cuda")
-    kc = cuda.zeros((nkv, ctx, hd), dtype=T, device="cuda")
-    vc = cuda.zeros((nkv, ctx, hd), dtype=T, device="cuda")
     c_t, s_t = cuda.from_numpy(cos).cuda(), cuda.from_numpy(sin).cuda()
-    ie.qkv(to_dev(d["x"], dt), to_dev(d["wq"], dt), to_dev(d["wk"], dt), to_dev(d["wv"], dt), q, kc, vc,
-           ctx * hd, pos0, c_t, s_t, n_q_heads=nq, n_kv_heads=nkv)
     qr, kr, vr = oracle.qkv(d["x"], d["wq"], d["wk"], d["wv"], dt, pos0, cos, sin)
-    for got, want, tol in zip((from_dev(q), from_dev(kc)[:, pos0:pos0 + M], from_dev(vc)[:, pos0:pos0 + M]),
-                              (qr, kr, vr), rope_tol(d["x"], d["wq"], d["wk"], d["wv"], dt, True)):
-        err = np.abs(got - want)
-        assert np.all(err <= tol), f"max err {err.max():.3g}, worst excess {(err - tol).max():.3g}"
-    kall = from_dev(kc)
-    mask = np.ones(ctx, bool)
-    mask[pos0:pos0 + M] = False
-    assert np.all(kall[:, mask] == 0)
+    tols = rope_tol(d["x"], d["wq"], d["wk"], d["wv"], dt, True)
+    x, wq, wk, wv = (to_dev(d[k], dt) for k in ("x", "wq", "wk", "wv"))
+    ws = ie.split_workspace()
+    for workspace in (None, ws):  # whole tiles, then the tail split
+        q = cuda.empty((nq, M, hd), dtype=T, device="cuda")
+        kc = cuda.zeros((nkv, ctx, hd), dtype=T, device="cuda")
+        vc = cuda.zeros((nkv, ctx, hd), dtype=T, device="cuda")
+        ie.qkv(x, wq, wk, wv, q, kc, vc, ctx * hd, pos0, c_t, s_t, n_q_heads=nq, n_kv_heads=nkv, workspace=workspace)
+        for got, want, tol in zip((from_dev(q), from_dev(kc)[:, pos0:pos0 + M], from_dev(vc)[:, pos0:pos0 + M]),
+                                  (qr, kr, vr), tols):
+            err = np.abs(got - want)
+            assert np.all(err <= tol), f"max err {err.max():.3g}, worst excess {(err - tol).max():.3g}"
+        kall = from_dev(kc)
+        mask = np.ones(ctx, bool)
+        mask[pos0:pos0 + M] = False
+        assert np.all(kall[:, mask] == 0)
+    assert_split_workspace_clean(ie, cuda, ws)
 
 
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
