@@ -18,7 +18,14 @@
 //    the same permutation of k, so no shuffles or shared-memory staging are
 //    needed to build fragments;
 //  * per-warp fp32 partials are summed across the 8 warps in shared memory in
-//    a fixed order (deterministic results), then one warp runs the epilogue.
+//    a fixed order (deterministic results), then one warp runs the epilogue;
+//  * when the tiles alone would leave most SMs idle (the column-split shards
+//    of tensor parallelism: QKV of 4+1+1 heads is 48 tiles at 8 GPUs), the
+//    K range of a tile is split over a thread-block cluster of 2 or 4 CTAs
+//    (ksplit). Each CTA reduces its warps as above, writes its partial tile
+//    into the leading CTA's shared memory through DSMEM, and after one
+//    cluster barrier the leader adds the partials in rank order and runs the
+//    epilogue. No global scratch and no spin-waits; still deterministic.
 #include "ie_common.cuh"
 #include "skinny.cuh"
 #include <cstdlib>
@@ -83,6 +90,7 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kWords = IE_SK_LOADW / 4;  // 32-bit words per lane per row per k-step
 constexpr int kStep = kWords * 2 * 4;    // k elements per step (4 lanes share a row)
 constexpr int kUnroll = IE_SK_UNROLL;
+constexpr int kMaxKSplit = 4;  // CTAs of one tile's cluster (K split)
 
 template <int EPI> struct EpiTraits { static constexpr int nmat = 1; };
 template <> struct EpiTraits<EPI_SWIGLU> { static constexpr int nmat = 2; };
@@ -376,6 +384,7 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? IE_SK_MINBLOCKS_MT1 : IE_S
   constexpr int NMAT = EpiTraits<EPI>::nmat;
   constexpr int NR = NMAT * MT * 4;
   __shared__ float red[kWarps][NR][32];
+  __shared__ float xred[kMaxKSplit][NR][32];  // cluster split: partial tile of every CTA (in the leader)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
 
@@ -388,8 +397,13 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? IE_SK_MINBLOCKS_MT1 : IE_S
     xrow[mt] = static_cast<const T*>(p.X) + (int64_t)(xvalid[mt] ? m : 0) * p.ldx;
   }
   const int nsteps = (p.K + kStep - 1) / kStep;
-  const int s_begin = (warp * nsteps) / kWarps;
-  const int s_end = ((warp + 1) * nsteps) / kWarps;
+  // cluster split: this CTA's share of the k-steps, then the warps' shares
+  unsigned int krank = 0;
+  if (p.ksplit > 1) asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(krank));
+  const int c_begin = ((int)krank * nsteps) / p.ksplit;
+  const int c_steps = (((int)krank + 1) * nsteps) / p.ksplit - c_begin;
+  const int s_begin = c_begin + (warp * c_steps) / kWarps;
+  const int s_end = c_begin + ((warp + 1) * c_steps) / kWarps;
   const uint64_t pol = policy_evict_first();
 
   // Programmatic dependent launch: activations (X) come from the previous
@@ -407,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? IE_SK_MINBLOCKS_MT1 : IE_S
   for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
 #else
   {
-    const int tile = blockIdx.x;
+    const int tile = p.ksplit > 1 ? (int)blockIdx.x / p.ksplit : (int)blockIdx.x;
 #endif
     const T* wrow[NMAT][2];
     bool rvalid[2];
@@ -514,9 +528,41 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? IE_SK_MINBLOCKS_MT1 : IE_S
             for (int w = 0; w < kWarps; ++w) sum += red[w][(mat * MT + mt) * 4 + i][lane];
             acc[mat][mt][i] = sum;
           }
-      epilogue<T, MT, EPI>(p, tile, g, t, lane, rvalid, nidx, acc);
     }
-    if constexpr (EPI == EPI_TP_ALLREDUCE) tp_finish<T>(p);
+    if (p.ksplit > 1) {
+      // every CTA of the cluster hands its partial tile to the leader (rank 0)
+      if (warp == 0) {
+        const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(&xred[krank][0][lane]));
+        uint32_t remote;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(base), "r"(0));
+#pragma unroll
+        for (int mat = 0; mat < NMAT; ++mat)
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote + (uint32_t)(((mat * MT + mt) * 4 + i) * 32 * 4)),
+                           "f"(acc[mat][mt][i])
+                           : "memory");
+      }
+      asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+      if (krank == 0 && warp == 0) {
+#pragma unroll
+        for (int mat = 0; mat < NMAT; ++mat)
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              float sum = xred[0][(mat * MT + mt) * 4 + i][lane];
+              for (int r = 1; r < p.ksplit; ++r) sum += xred[r][(mat * MT + mt) * 4 + i][lane];
+              acc[mat][mt][i] = sum;
+            }
+      }
+    }
+    if (warp == 0 && krank == 0) epilogue<T, MT, EPI>(p, tile, g, t, lane, rvalid, nidx, acc);
+    if constexpr (EPI == EPI_TP_ALLREDUCE) {
+      if (krank == 0) tp_finish<T>(p);
+    }
 #if IE_SK_PERSIST
     __syncthreads();  // red is reused by the next tile
 #endif
@@ -629,17 +675,28 @@ static bool pdl_enabled() {
 }
 
 template <typename K, typename... Args>
-static cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+static cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, cudaStream_t st, int cluster, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
@@ -657,10 +714,38 @@ static int resident_ctas(K kernel) {
   return (sms > 0 ? sms : 148) * (per_sm > 0 ? per_sm : 1);
 }
 
+// K split over a cluster (SkinnyParams::ksplit): doubled (up to 4) while
+// the grid still fits twice per SM and every CTA keeps >= 1024 elements of K.
+// Depends only on the tile count and K, never on M, so a row gets the same
+// bits alone and in a batch. IE_SK_KSPLIT=1, 2 or 4 in the environment fixes
+// the split instead (where K allows 512 elements per CTA).
+static int ksplit_for(int tiles, int K) {
+  static const int forced = [] {
+    const char* e = getenv("IE_SK_KSPLIT");
+    const int v = e ? atoi(e) : 0;
+    return (v == 1 || v == 2 || v == 4) ? v : 0;
+  }();
+  if (IE_SK_PERSIST) return 1;
+  if (forced) {
+    int s = forced;
+    while (s > 1 && K / s < 512) s /= 2;
+    return s;
+  }
+  static const int slots = [] {
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return 2 * (sms > 0 ? sms : 148);
+  }();
+  int s = 1;
+  while (s < kMaxKSplit && (int64_t)tiles * s * 2 <= slots && K / (s * 2) >= 1024) s *= 2;
+  return s;
+}
+
 template <typename T, int MT, int EPI>
 static cudaError_t launch_variant(const SkinnyParams& p, cudaStream_t st) {
   auto kernel = skinny_kernel<T, MT, EPI>;
-  int grid = p.tiles;
+  int grid = p.tiles * p.ksplit;
   if constexpr (EPI == EPI_TP_ALLREDUCE) {
     // every CTA waits for the same tile of the other ranks: all must fit at once
     static const int resident = resident_ctas(kernel);
@@ -670,7 +755,7 @@ static cudaError_t launch_variant(const SkinnyParams& p, cudaStream_t st) {
   static const int resident = resident_ctas(kernel);
   grid = p.tiles < resident ? p.tiles : resident;
 #endif
-  return launch_pdl(kernel, dim3(grid), dim3(kThreads), st, p);
+  return launch_pdl(kernel, dim3(grid), dim3(kThreads), st, p.ksplit, p);
 }
 
 template <typename T, int EPI>
@@ -682,6 +767,7 @@ static cudaError_t launch_skinny_t(const SkinnyParams& p0, int tiles, cudaStream
              (EPI != EPI_QKV || p.n_kv_heads == 0 || (rows_wide(p.W1, p.ldw) && rows_wide(p.W2, p.ldw)));
   p.x_wide = rows_wide(p.X, p.ldx);
   p.early_w = p.M <= IE_SK_EARLY_W_MAX_M;
+  p.ksplit = ksplit_for(tiles, p.K);
   if (p.M <= 8) return launch_variant<T, 1, EPI>(p, st);
   return launch_variant<T, 2, EPI>(p, st);
 }

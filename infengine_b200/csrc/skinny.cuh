@@ -41,6 +41,8 @@ struct SkinnyParams {
   // programmatic-launch wait (few activation rows)
   bool early_w = false;
   int tiles = 0;
+  // set by launch_skinny: CTAs (one cluster) that split the K range of a tile
+  int ksplit = 1;
   void* Y = nullptr;
   int64_t ldy = 0;
   // EPI_STORE / EPI_TP_ALLREDUCE: Y = round(Y + round(result)), the residual

@@ -48,6 +48,11 @@ def assert_within_one_rounding(got, gold_fp32, dt):
     (9, 272, 520),        # second n8 tile, K not a multiple of 32
     (16, 128, 8),         # smallest legal K
     (7, 33, 1032),
+    # few tiles: the K range is split over a cluster of 2 or 4 CTAs
+    (1, 512, 4096),       # 32 tiles, 4-way (a Q shard of 4 heads)
+    (8, 1792, 4096),      # 112 tiles, 2-way (a gate or up shard at 8 GPUs)
+    (3, 1024, 14336),     # 64 tiles, 4-way, long K
+    (16, 240, 2056),      # 15 tiles, 2-way, K not a multiple of the chunk
 ])
 def test_gemm_skinny(ie, cuda, dt, M, N, K):
     d = oracle.seeded_inputs(M * 1000 + N + K, {"x": (M, K), "w": (N, K)}, dt)
@@ -55,6 +60,23 @@ def test_gemm_skinny(ie, cuda, dt, M, N, K):
     ie.gemm(to_dev(d["x"], dt), to_dev(d["w"], dt), y)
     got = from_dev(y)
     assert_within_one_rounding(got, oracle.gemm_fp32(d["x"], d["w"]), dt)
+
+
+@pytest.mark.parametrize("N,K", [(512, 4096), (1792, 4096), (4096, 4096)])
+def test_gemm_skinny_rows_batch_invariant(ie, cuda, N, K):
+    """A row gets the same bits alone and inside batches of 3, 8 and 16 rows,
+    with and without the cluster K split (which depends on N and K only)."""
+    dt = "bf16"
+    d = oracle.seeded_inputs(N + K, {"x": (16, K), "w": (N, K)}, dt)
+    x, w = to_dev(d["x"], dt), to_dev(d["w"], dt)
+    T = torch_dtype(dt)
+    alone = cuda.empty((1, N), dtype=T, device="cuda")
+    ie.gemm(x[:1], w, alone)
+    for M in (3, 8, 16):
+        y = cuda.empty((M, N), dtype=T, device="cuda")
+        ie.gemm(x[:M], w, y)
+        cuda.cuda.synchronize()
+        assert cuda.equal(y[0], alone[0]), M
 
 
 @pytest.mark.parametrize("dt", DTS)
@@ -84,10 +106,11 @@ def test_gemm_strided_operands(ie, cuda):
 
 
 @pytest.mark.parametrize("dt", DTS)
-@pytest.mark.parametrize("M", [1, 4, 8])
-def test_ffn_decode_config2(ie, cuda, dt, M):
-    """Llama-3.1-8B FFN at decode, M in {1,4,8}."""
-    H, F = 4096, 14336
+@pytest.mark.parametrize("M,F", [(1, 14336), (4, 14336), (8, 14336), (1, 1792), (8, 3584)])
+def test_ffn_decode_config2(ie, cuda, dt, M, F):
+    """Llama-3.1-8B FFN at decode, M in {1,4,8}; and the
+    FFN shards of 8 and 4 GPUs (gate/up split over 2-CTA clusters)."""
+    H = 4096
     d = oracle.seeded_inputs(100 + M, {"x": (M, H), "wg": (F, H), "wu": (F, H), "wd": (H, F)}, dt,
                              scales={"wg": 0.02, "wu": 0.02, "wd": 0.02})
     ws = cuda.empty(ie.ffn_workspace_bytes(M, F), dtype=cuda.uint8, device="cuda")
@@ -111,9 +134,12 @@ def test_ffn_decode_config2(ie, cuda, dt, M):
 
 
 @pytest.mark.parametrize("dt", DTS)
-@pytest.mark.parametrize("M,pos0,rope", [(1, 2047, True), (5, 100, True), (3, 0, False), (16, 8000, True)])
-def test_qkv_fused(ie, cuda, dt, M, pos0, rope):
-    H, nq, nkv, hd, ctx = 4096, 32, 8, 128, 8192
+@pytest.mark.parametrize("M,pos0,rope,nq,nkv", [(1, 2047, True, 32, 8), (5, 100, True, 32, 8), (3, 0, False, 32, 8),
+                                                (16, 8000, True, 32, 8),
+                                                (1, 2047, True, 4, 1),    # 8-GPU shard: 48 tiles, 4-way K split
+                                                (5, 300, True, 8, 2)])    # 4-GPU shard: 96 tiles, 2-way
+def test_qkv_fused(ie, cuda, dt, M, pos0, rope, nq, nkv):
+    H, hd, ctx = 4096, 128, 8192
     d = oracle.seeded_inputs(7 + M, {"x": (M, H), "wq": (nq * hd, H), "wk": (nkv * hd, H), "wv": (nkv * hd, H)}, dt)
     cos, sin = oracle.rope_tables(ctx)
     T = torch_dtype(dt)
@@ -123,7 +149,7 @@ def test_qkv_fused(ie, cuda, dt, M, pos0, rope):
     c_t = cuda.from_numpy(cos).cuda() if rope else None
     s_t = cuda.from_numpy(sin).cuda() if rope else None
     ie.qkv(to_dev(d["x"], dt), to_dev(d["wq"], dt), to_dev(d["wk"], dt), to_dev(d["wv"], dt), q, kc, vc,
-           ctx * hd, pos0, c_t, s_t)
+           ctx * hd, pos0, c_t, s_t, n_q_heads=nq, n_kv_heads=nkv)
     qr, kr, vr = oracle.qkv(d["x"], d["wq"], d["wk"], d["wv"], dt, pos0, cos if rope else None,
                             sin if rope else None)
     got_q = from_dev(q)
