@@ -499,22 +499,25 @@ def single_case(torch, name: str, steps: int, seed: int):
         ws = torch.zeros(ie.lm_head_workspace_bytes(1), dtype=torch.uint8, device=dev)
         tok = torch.zeros(1, dtype=torch.int32, device=dev)
         fn = lambda: ie.lm_head_argmax(x, lm, ws, idx_out=tok)
-    elif name in ("engine_decode", "engine_small"):
-        # the whole model through the engine: a 2048-token prefill, then
-        # `steps` decode steps (graph replays); engine_small keeps 2 of the 32
-        # layers so that a full ncu capture holds a few GB, not 17
-        n_layers = L if name == "engine_decode" else 2
+    elif name in ("engine_decode", "engine_small", "engine_decode_bs8"):
+        # the whole model through the engine: a 2048-token prefill (of each
+        # of 8 sequences for engine_decode_bs8), then `steps` decode steps
+        # (graph replays); engine_small keeps 2 of the 32 layers so that a
+        # full ncu capture holds a few GB, not 17
+        n_layers = 2 if name == "engine_small" else L
+        batch = 8 if name == "engine_decode_bs8" else 1
         layers = [{"wq": w(NQ * HD, H), "wk": w(NKV * HD, H), "wv": w(NKV * HD, H), "wo": w(H, H),
                    "wg": w(F, H), "wu": w(F, H), "wd": w(H, F)} for _ in range(n_layers)]
         weights = full_model_weights(torch, dev, seed, layers, w(V, H))
         from infengine_b200.engine import LlamaEngine
         dims = dict(n_layers=n_layers, hidden=H, n_q_heads=NQ, n_kv_heads=NKV, head_dim=HD, ffn_dim=F, vocab=V)
-        eng = LlamaEngine(weights, dims, max_batch=1, max_ctx=PROMPT + steps + 16, max_prefill=PROMPT)
-        eng.prefill(0, prompts(seed, 1)[0])
+        eng = LlamaEngine(weights, dims, max_batch=batch, max_ctx=PROMPT + steps + 16, max_prefill=PROMPT)
+        for b, pr in enumerate(prompts(seed, batch)):
+            eng.prefill(b, pr)
         eng.decode(steps)
         eng.close()
         torch.cuda.synchronize()
-        print(json.dumps({"case": name, "layers": n_layers, "decode_steps": steps}))
+        print(json.dumps({"case": name, "layers": n_layers, "batch": batch, "decode_steps": steps}))
         return
     elif name == "prefill_attention":
         # the attention core of a 2048-token prefill: causal 2048 x 2048, 32
@@ -936,8 +939,9 @@ def main():
     ap.add_argument("--case", default=None,
                     help="for profiling: one kernel (gate_up|down|o|qkv|lm_head|prefill_{qkv,o,gate_up,down}|"
                          "prefill_attention) "
-                         "--steps times, or the engine (engine_decode: 32 layers, engine_small: 2 layers) with a "
-                         "2048-token prefill and --steps decode steps")
+                         "--steps times, or the engine (engine_decode: 32 layers, engine_small: 2 layers, "
+                         "engine_decode_bs8: 32 layers, 8 sequences) with a 2048-token prefill per sequence and "
+                         "--steps decode steps")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

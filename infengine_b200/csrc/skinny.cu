@@ -89,7 +89,15 @@ constexpr int kThreads = kWarps * 32;
 #endif
 constexpr int kWords = IE_SK_LOADW / 4;  // 32-bit words per lane per row per k-step
 constexpr int kStep = kWords * 2 * 4;    // k elements per step (4 lanes share a row)
-constexpr int kUnroll = IE_SK_UNROLL;
+#ifndef IE_SK_UNROLL_ONE
+// k-steps per batch for one weight matrix and at most 8 activation rows: the
+// registers these variants leave free (88 of 128 at 2 CTAs per SM) hold a
+// batch twice as deep, which doubles the weight bytes in flight per warp.
+#define IE_SK_UNROLL_ONE 4
+#endif
+// k-steps whose loads are issued together, per variant
+template <int NMAT, int MT>
+struct Unroll { static constexpr int value = (NMAT == 1 && MT == 1) ? IE_SK_UNROLL_ONE : IE_SK_UNROLL; };
 constexpr int kMaxKSplit = 4;  // CTAs of one tile's cluster (K split)
 
 template <int EPI> struct EpiTraits { static constexpr int nmat = 1; };
@@ -365,12 +373,13 @@ __device__ __forceinline__ void ld_chunk(const void* row, int k, int K, bool val
   }
 }
 
-// Registers of one load batch: kUnroll k-steps of two rows per weight matrix
+// Registers of one load batch: UNR k-steps of two rows per weight matrix
 // and of the activation row(s).
 template <int NMAT, int MT>
 struct Batch {
-  uint32_t w[kUnroll][NMAT][2][kWords];
-  uint32_t x[kUnroll][MT][kWords];
+  static constexpr int UNR = Unroll<NMAT, MT>::value;
+  uint32_t w[UNR][NMAT][2][kWords];
+  uint32_t x[UNR][MT][kWords];
 };
 
 // Grid = one CTA per 16-row tile (IE_SK_PERSIST = 0) or a persistent grid of
@@ -379,10 +388,13 @@ struct Batch {
 // loads of its next batch before the MMAs of the current one, so it always
 // has loads in flight.
 template <typename T, int MT, int EPI>
-__global__ void __launch_bounds__(kThreads, MT == 1 ? IE_SK_MINBLOCKS_MT1 : IE_SK_MINBLOCKS)
+__global__ void __launch_bounds__(kThreads, (MT == 1 && EpiTraits<EPI>::nmat == 1 && IE_SK_UNROLL_ONE > IE_SK_UNROLL)
+                                                ? 2
+                                                : (MT == 1 ? IE_SK_MINBLOCKS_MT1 : IE_SK_MINBLOCKS))
     skinny_kernel(const SkinnyParams p) {
   constexpr int NMAT = EpiTraits<EPI>::nmat;
   constexpr int NR = NMAT * MT * 4;
+  constexpr int kUnroll = Unroll<NMAT, MT>::value;
   __shared__ float red[kWarps][NR][32];
   __shared__ float xred[kMaxKSplit][NR][32];  // cluster split: partial tile of every CTA (in the leader)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
