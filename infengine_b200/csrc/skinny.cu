@@ -181,36 +181,63 @@ __device__ __forceinline__ void epilogue(const SkinnyParams& p, int tile, int g,
     unsigned long long t0;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
     bool gave_up = false;
+    // A lane's words are polled in passes, two values (batch rows m, m+1 of
+    // one output column) at a time: each pass issues the loads of every word
+    // of the pair still missing, from all ranks, back to back and only then
+    // checks them, so a pass costs about one memory round trip whatever the
+    // number of ranks (polling rank after rank cost one round trip per rank).
+#pragma unroll 1
+    for (int grp = 0; grp < 2 * MT && !gave_up; ++grp) {
+      const int mt = grp >> 1, r = grp & 1;
+      const unsigned long long* w[2];
+      unsigned int missing[2];
+      float part[2][kTpMaxWorld];
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+      for (int j = 0; j < 2; ++j) {
+        const int m = mt * 8 + 2 * t + j;
+        const bool valid = rvalid[r] && m < p.M;
+        w[j] = inbox + (size_t)(valid ? m : 0) * p.tp_cols + nidx[r];
+        missing[j] = valid ? (1u << p.tp_world) - 1u : 0u;
+      }
+      while ((missing[0] | missing[1]) != 0u) {
+        unsigned long long got[2][kTpMaxWorld];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = i >> 1, m = mt * 8 + 2 * t + (i & 1);
-        if (!rvalid[r] || m >= p.M || gave_up) continue;
-        float sum = 0.f;
-        for (int q = 0; q < p.tp_world && !gave_up; ++q) {
-          const unsigned long long* w = inbox + (size_t)q * slot + (size_t)m * p.tp_cols + nidx[r];
-          while (true) {
-            unsigned long long v;
-            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(w) : "memory");
-            if ((unsigned int)(v >> 32) == e) {
-              sum += __uint_as_float((unsigned int)(v & 0xffffffffull));
-              break;
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int q = 0; q < kTpMaxWorld; ++q)
+            if ((missing[j] >> q) & 1u)
+              asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(got[j][q]) : "l"(w[j] + (size_t)q * slot)
+                           : "memory");
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int q = 0; q < kTpMaxWorld; ++q)
+            if (((missing[j] >> q) & 1u) && (unsigned int)(got[j][q] >> 32) == e) {
+              part[j][q] = __uint_as_float((unsigned int)(got[j][q] & 0xffffffffull));
+              missing[j] &= ~(1u << q);
             }
-            unsigned long long now;
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-            if (now - t0 > limit) {
-              atomicExch(&g_skinny_status, IE_ERR_TIMEOUT);
-              gave_up = true;
-              break;
-            }
-          }
-        }
-        if (!gave_up) {
-          T* y = Y + (int64_t)m * p.ldy + nidx[r];
-          *y = DT<T>::from_f(p.residual ? DT<T>::to_f(*y) + round_to<T>(sum) : sum);
+        if ((missing[0] | missing[1]) == 0u) break;
+        unsigned long long now;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+        if (now - t0 > limit) {
+          atomicExch(&g_skinny_status, IE_ERR_TIMEOUT);
+          gave_up = true;
+          break;
         }
       }
+      if (gave_up) break;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int m = mt * 8 + 2 * t + j;
+        if (!rvalid[r] || m >= p.M) continue;
+        float sum = 0.f;  // rank order, as always
+#pragma unroll
+        for (int q = 0; q < kTpMaxWorld; ++q)
+          if (q < p.tp_world) sum += part[j][q];
+        T* y = Y + (int64_t)m * p.ldy + nidx[r];
+        *y = DT<T>::from_f(p.residual ? DT<T>::to_f(*y) + round_to<T>(sum) : sum);
+      }
+    }
   } else if constexpr (EPI == EPI_STORE_F32) {
     float* Y = static_cast<float*>(p.Y);
 #pragma unroll
@@ -388,7 +415,10 @@ struct Batch {
 // loads of its next batch before the MMAs of the current one, so it always
 // has loads in flight.
 template <typename T, int MT, int EPI>
-__global__ void __launch_bounds__(kThreads, (MT == 1 && EpiTraits<EPI>::nmat == 1 && IE_SK_UNROLL_ONE > IE_SK_UNROLL)
+// (2 CTAs per SM are kept for the deeper one-matrix batches and for the
+// exchange kernel, whose whole grid must be resident at once)
+__global__ void __launch_bounds__(kThreads, ((MT == 1 && EpiTraits<EPI>::nmat == 1 && IE_SK_UNROLL_ONE > IE_SK_UNROLL) ||
+                                             EPI == EPI_TP_ALLREDUCE)
                                                 ? 2
                                                 : (MT == 1 ? IE_SK_MINBLOCKS_MT1 : IE_SK_MINBLOCKS))
     skinny_kernel(const SkinnyParams p) {
