@@ -519,6 +519,39 @@ def single_case(torch, name: str, steps: int, seed: int):
         torch.cuda.synchronize()
         print(json.dumps({"case": name, "layers": n_layers, "batch": batch, "decode_steps": steps}))
         return
+    elif name in ("decode_attention_bs1", "decode_attention_bs8"):
+        # the decode attention core of one step at position 2047 (after the
+        # 2048-token prompt): B sequences x 8 KV heads, 32 layers' caches so
+        # that the keys and values stream from HBM as in the engine (67 MB a
+        # layer at B = 8); timed as one graph of 32 launches
+        B = 8 if name.endswith("bs8") else 1
+        rows = PROMPT + 64
+        q = torch.randn(NQ, B, HD, generator=g, device=dev, dtype=torch.float32).to(bf)
+        kcs = [torch.randn(B, NKV, rows, HD, generator=g, device=dev, dtype=torch.float32).to(bf) for _ in range(L)]
+        vcs = [torch.randn(B, NKV, rows, HD, generator=g, device=dev, dtype=torch.float32).to(bf) for _ in range(L)]
+        pos = torch.full((B,), PROMPT - 1, dtype=torch.int32, device=dev)
+        out = torch.empty(B, NQ * HD, device=dev, dtype=bf)
+        st = torch.cuda.Stream()
+        run = lambda: [ie.attention_decode(q, kcs[l], vcs[l], out, positions=pos, stream=st) for l in range(L)]
+        with torch.cuda.stream(st):
+            run()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=st):
+            run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st):
+            gr.replay()
+            e0.record(st)
+            for _ in range(steps):
+                gr.replay()
+            e1.record(st)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (steps * L)
+        kv = 2 * B * NKV * PROMPT * HD * 2
+        print(json.dumps({"case": name, "launches": (steps + 1) * L, "us_per_launch": round(us, 2),
+                          "kv_bytes": kv, "gbs": round(kv / us / 1e3, 1)}))
+        return
     elif name == "prefill_attention":
         # the attention core of a 2048-token prefill: causal 2048 x 2048, 32
         # query / 8 KV heads (K/V of one layer: 8 MB, L2-resident like in the
@@ -938,7 +971,7 @@ def main():
                     help="skip timing the reference's own kernels per BASELINE config")
     ap.add_argument("--case", default=None,
                     help="for profiling: one kernel (gate_up|down|o|qkv|lm_head|prefill_{qkv,o,gate_up,down}|"
-                         "prefill_attention) "
+                         "prefill_attention|decode_attention_bs1|decode_attention_bs8) "
                          "--steps times, or the engine (engine_decode: 32 layers, engine_small: 2 layers, "
                          "engine_decode_bs8: 32 layers, 8 sequences) with a 2048-token prefill per sequence and "
                          "--steps decode steps")

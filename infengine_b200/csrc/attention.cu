@@ -67,8 +67,9 @@ namespace {
 constexpr int kFdThreads = 256;
 constexpr int kFdWarps = kFdThreads / 32;
 constexpr int kFdRows = 64;
-constexpr int kFdStages = 6;
-constexpr int kFdRingBytes = kFdStages * kFdRows * 128 * 2;
+constexpr int kFdStages = 6;  // deepest ring (the size limits are checked against it)
+constexpr int kFdStageBytes = kFdRows * 128 * 2;
+constexpr int kFdRingBytes = kFdStages * kFdStageBytes;
 
 struct FdParams {
   const void* q;
@@ -81,7 +82,8 @@ struct FdParams {
   int pos0, rows_per_seq;
   void* out;
   int64_t ld_out;
-  int cap;  // score slots per head in shared memory (>= ceil(cache_rows / 8))
+  int cap;     // score slots per head in shared memory (>= ceil(cache_rows / 8))
+  int stages;  // ring depth in 64-row chunks, 2 .. kFdStages (occupancy only; no effect on the results)
 };
 
 __device__ __forceinline__ uint32_t fd_smem_u32(const void* p) {
@@ -166,7 +168,8 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
   __shared__ int abort_s, fail_at;
 
   T* ring = reinterpret_cast<T*>(fd_smem);
-  T* sc = reinterpret_cast<T*>(fd_smem + kFdRingBytes);
+  const int S = p.stages;
+  T* sc = reinterpret_cast<T*>(fd_smem + S * kFdStageBytes);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   unsigned rank;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
@@ -199,7 +202,7 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
   auto arm = [&](int i) {
     int r0, rows;
     chunk_of(i, r0, rows);
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(fd_smem_u32(&bars[i % kFdStages])),
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(fd_smem_u32(&bars[i % S])),
                  "r"((uint32_t)rows * 128u * (uint32_t)sizeof(T))
                  : "memory");
     issued = i + 1;
@@ -211,7 +214,7 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
     lo = max(lo, r0);
     hi = min(hi, r0 + rows);
     if (hi <= lo) return;
-    const int slot = i % kFdStages;
+    const int slot = i % S;
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      fd_smem_u32(ring + (slot * kFdRows + (lo - r0)) * 128)),
                  "l"((i < nk ? kh : vh) + (int64_t)lo * 128), "r"((uint32_t)(hi - lo) * 128u * (uint32_t)sizeof(T)),
@@ -223,9 +226,9 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
     copy(i, 0, INT_MAX);
   };
 
-  const int first = min(kFdStages, total);
+  const int first = min(S, total);
   if (tid == 0) {
-    for (int s = 0; s < kFdStages; ++s)
+    for (int s = 0; s < S; ++s)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(fd_smem_u32(&bars[s])) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     abort_s = 0;
@@ -262,12 +265,12 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
     }
 
   auto wait_chunk = [&](int i) {
-    if (!fd_wait(fd_smem_u32(&bars[i % kFdStages]), (uint32_t)((i / kFdStages) & 1), &abort_s))
+    if (!fd_wait(fd_smem_u32(&bars[i % S]), (uint32_t)((i / S) & 1), &abort_s))
       atomicMin(&fail_at, i);
   };
   auto next = [&](int i) {
-    __syncthreads();  // every warp is done with slot i % kFdStages
-    if (tid == 0 && !abort_s && i + kFdStages < total) issue(i + kFdStages);
+    __syncthreads();  // every warp is done with slot i % S
+    if (tid == 0 && !abort_s && i + S < total) issue(i + S);
   };
 
   // ---- scores on the tensor cores: S[row][head] = K[row] . q[head], one
@@ -276,7 +279,7 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
   const float scale = rsqrtf(128.0f);
   for (int i = 0; i < nk; ++i) {
     wait_chunk(i);
-    const T* tile = ring + (i % kFdStages) * kFdRows * 128;
+    const T* tile = ring + (i % S) * kFdRows * 128;
     const int r0 = i * kFdRows, rows = min(kFdRows, n - r0);
     float c[4] = {0.f, 0.f, 0.f, 0.f};
     const T* ra = tile + (tile_w * 16 + fg) * 128 + 64 * half_w + 8 * ft;
@@ -381,7 +384,7 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
     for (int d = 0; d < 4; ++d) acc[h][d] = 0.f;
   for (int i = nk; i < total; ++i) {
     wait_chunk(i);
-    const T* tile = ring + (i % kFdStages) * kFdRows * 128;
+    const T* tile = ring + (i % S) * kFdRows * 128;
     const int r0 = (i - nk) * kFdRows, rows = min(kFdRows, n - r0);
 #pragma unroll 4
     for (int r = warp; r < rows; r += kFdWarps) {
@@ -400,7 +403,7 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
   if (tid == 0 && fail_at < issued) {
     for (int i = fail_at; i < issued; ++i) {
       const unsigned long long t0 = fd_now();
-      while (!fd_try(fd_smem_u32(&bars[i % kFdStages]), (uint32_t)((i / kFdStages) & 1)) &&
+      while (!fd_try(fd_smem_u32(&bars[i % S]), (uint32_t)((i / S) & 1)) &&
              fd_now() - t0 < kDrainWaitNs) {
       }
     }
@@ -436,7 +439,7 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
 template <typename T, int G, int C>
 cudaError_t launch_decode_attention(const FdParams& p, int n_kv_heads, int R, cudaStream_t st) {
   auto kernel = decode_attention_kernel<T, G, C>;
-  const size_t smem = kFdRingBytes + (size_t)G * p.cap * sizeof(T);
+  const size_t smem = (size_t)p.stages * kFdStageBytes + (size_t)G * p.cap * sizeof(T);
   static size_t configured[64] = {};  // per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -463,6 +466,35 @@ cudaError_t launch_decode_attention(const FdParams& p, int n_kv_heads, int R, cu
   const char* env = getenv("IE_PDL");
   cfg.numAttrs = (env && env[0] == '0') ? 1 : 2;
   return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
+// Ring depth of a launch: the full 6 stages while the grid fits twice per SM,
+// else the deepest ring that lets every CTA be resident at once (the ring is
+// most of a CTA's shared memory), at least 2 (the CTA partials reuse 32 KB of
+// it). Only residency depends on it: which warp adds which cache row, and so
+// every result bit, comes from the 64-row chunks. IE_FD_STAGES=2..6 in the
+// environment fixes it (for measurements).
+int fd_stages(int ctas, int group, int cap) {
+  static const int forced = [] {
+    const char* e = getenv("IE_FD_STAGES");
+    const int v = e ? atoi(e) : 0;
+    return (v >= 2 && v <= kFdStages) ? v : 0;
+  }();
+  if (forced) return forced;
+  static const int sms = [] {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+  }();
+  const int per_sm = (ctas + sms - 1) / sms;
+  if (per_sm <= 2) return kFdStages;
+  // static shared memory of the kernel (q, partials, scores scratch) and a
+  // reserve, against the 227 KB a B200 SM offers
+  const size_t fixed = (size_t)group * 128 * 4 * 2 + (size_t)2 * kFdRows * group * 4 + 2048 + 1024;
+  for (int s = kFdStages; s > 2; --s)
+    if ((size_t)per_sm * ((size_t)s * kFdStageBytes + (size_t)group * cap * 2 + fixed) <= 227u * 1024u) return s;
+  return 2;
 }
 
 // Cluster size from the KV head count alone: 16 CTAs per (row, KV head) for
@@ -539,6 +571,7 @@ extern "C" int ie_attention_decode(ie_dtype dt, int R, int rows_per_seq, int n_q
   // score slots per head: the 8-CTA slice bound serves both cluster sizes
   p.cap = ((cache_rows + 8 - 1) / 8 + 7) / 8 * 8;
   if (kFdRingBytes + (size_t)group * p.cap * 2 > 200 * 1024) return IE_ERR_UNSUPPORTED;
+  p.stages = fd_stages(C * n_kv_heads * R, group, p.cap);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e;
 #define IE_FD(T, CL)                                                                   \
