@@ -893,8 +893,32 @@ def parity_leg(torch, dev, seed, n_steps, batch=8):
         out["max_miss_margin_ulps"] = max((x["margin_in_ulps"] for x in allm), default=None)
     finally:
         R.model_free()
+    out["reference_vs_itself"] = reference_noise_floor(seed, ps[0], ref_ids[0], ref_m[0], ref_top[0])
     out["seconds"] = round(time.perf_counter() - t_start, 1)
     return out
+
+
+def reference_noise_floor(seed, prompt, ids, margin, top):
+    """The reference's decode loop once more, in a second process whose
+    cuBLAS runs with CUBLAS_WORKSPACE_CONFIG=:0:0 (so it chooses other
+    kernels and split-K reductions), teacher-forced on the first run's ids
+    (oracle/ref_replay.py): how many greedy ids the reference itself changes
+    when only its fp32 summation order changes."""
+    with tempfile.TemporaryDirectory() as td:
+        pp, fp, op = (os.path.join(td, n) for n in ("prompt.npy", "forced.npy", "out.npz"))
+        np.save(pp, prompt)
+        np.save(fp, ids)
+        env = dict(os.environ, CUBLAS_WORKSPACE_CONFIG=":0:0")
+        r = subprocess.run([sys.executable, str(ROOT / "oracle" / "ref_replay.py"), str(seed), pp, fp, op], env=env,
+                           stdout=subprocess.DEVNULL, stderr=subprocess.PIPE, text=True)
+        if r.returncode != 0:
+            return {"error": r.stderr.strip().splitlines()[-1:] or ["replay failed"]}
+        got = np.load(op)["ids"]
+    bad = np.nonzero(got != ids)[0]
+    return {"teacher_forced_equal": int(len(ids) - len(bad)), "of": int(len(ids)),
+            "miss_margins_in_ulps": [round(float(margin[i]) / fp16_spacing(float(top[i])), 2) for i in bad],
+            "how": "the reference's loop in a second process with CUBLAS_WORKSPACE_CONFIG=:0:0, fed the first "
+                   "run's ids: the ids that change when only cuBLAS's kernel choice (summation order) changes"}
 
 
 def tp_parity(torch, dist, dev, seed, rank, prompt, tp_eng, tp_ids, ctx):
