@@ -154,6 +154,20 @@ __device__ __forceinline__ bool wait_count(const unsigned int* f, unsigned int t
   __syncwarp();
   return ok != 0;
 }
+// 32 entries of a RoPE table row (position pos, dimensions 32c .. 32c+31) as
+// 16-byte vectors (tables are 16-byte aligned, rows 256 bytes).
+__device__ __forceinline__ void load_rope32(const float* cos_t, const float* sin_t, int pos, int c, float (&cs)[32],
+                                            float (&sn)[32]) {
+  const float4* cp = reinterpret_cast<const float4*>(cos_t + (int64_t)pos * 64 + c * 32);
+  const float4* sp = reinterpret_cast<const float4*>(sin_t + (int64_t)pos * 64 + c * 32);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 a4 = __ldg(cp + j), b4 = __ldg(sp + j);
+    cs[4 * j] = a4.x; cs[4 * j + 1] = a4.y; cs[4 * j + 2] = a4.z; cs[4 * j + 3] = a4.w;
+    sn[4 * j] = b4.x; sn[4 * j + 1] = b4.y; sn[4 * j + 2] = b4.z; sn[4 * j + 3] = b4.w;
+  }
+}
+
 // Partial tile in the workspace (128 x 256 fp32 = 128 KB), laid out as
 // [32-column chunk c][float4 group i of the chunk][row][4]: the 32 rows of an
 // epilogue warp then read or write 512 contiguous bytes per access. Accessed
@@ -357,11 +371,28 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
     Unit u;
     for (int q = 0; !*abort_flag && unit_at<SPLIT>(args, q, u); ++q) {
       const int mb = u.tile % args.nm, nb = u.tile / args.nm;
+      const int m = mb * BM + row;
+      const bool mvalid = m < p.M;
+      // QKV: this row's position and the first half of its RoPE table rows
+      // (shared by the tile's two heads) are fetched while the MMAs run
+      int qpos = 0;
+      bool qrow_ok = mvalid;
+      float rcos[32], rsin[32];
+      if constexpr (EPI == TC_EPI_QKV) {
+        qpos = p.pos0 + m;
+        if (p.positions && mvalid) {
+          qpos = p.positions[m];
+          if (qpos < 0 || qpos >= p.cache_rows) {
+            atomicExch(&g_tc_status, IE_ERR_INVALID_ARG);
+            qrow_ok = false;
+            qpos = 0;
+          }
+        }
+        if (p.rope_cos && qrow_ok) load_rope32(p.rope_cos, p.rope_sin, qpos, 0, rcos, rsin);
+      }
       if (!mbar_wait(accf_bar(acc), acc_phase, abort_flag)) break;
       fence_after();
       const uint32_t tbase = tmem + acc * BN + ((uint32_t)(quad * 32) << 16);
-      const int m = mb * BM + row;
-      const bool mvalid = m < p.M;
       float v[32];
       // tail split: ranges 0 .. s-2 hand their partial sums to range s-1
       bool producer = false;
@@ -442,68 +473,53 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
           if (mvalid) store_row32<T>(drow, nb * 128 + c * 32, p.N, v);
         }
       } else if constexpr (EPI == TC_EPI_QKV) {
-        float b[32];
-#pragma unroll 1
+        // the tile's two heads (the second absent for an odd head count)
+        T* dsth[2] = {nullptr, nullptr};
+        bool ropeh[2] = {false, false};
+        const int64_t cb = p.positions ? (int64_t)m * p.cache_batch_stride : 0;
+#pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int head = 2 * nb + h;
-          if (head >= args.heads) break;
-          T* dst;
-          bool rope;
-          int pos = p.pos0 + m;
-          bool row_ok = mvalid;
-          if (p.positions && mvalid) {
-            pos = p.positions[m];
-            if (pos < 0 || pos >= p.cache_rows) {
-              atomicExch(&g_tc_status, IE_ERR_INVALID_ARG);
-              row_ok = false;
-              pos = 0;
-            }
-          }
-          const int64_t cb = p.positions ? (int64_t)m * p.cache_batch_stride : 0;
+          if (head >= args.heads) continue;
           if (head < p.n_q_heads) {
-            dst = static_cast<T*>(p.q_out) + (int64_t)head * p.q_head_stride + (int64_t)m * 128;
-            rope = p.rope_cos != nullptr;
+            dsth[h] = static_cast<T*>(p.q_out) + (int64_t)head * p.q_head_stride + (int64_t)m * 128;
+            ropeh[h] = p.rope_cos != nullptr;
           } else if (head < p.n_q_heads + p.n_kv_heads) {
-            dst = static_cast<T*>(p.k_cache) + cb + (int64_t)(head - p.n_q_heads) * p.cache_head_stride +
-                  (int64_t)pos * 128;
-            rope = p.rope_cos != nullptr;
+            dsth[h] = static_cast<T*>(p.k_cache) + cb + (int64_t)(head - p.n_q_heads) * p.cache_head_stride +
+                      (int64_t)qpos * 128;
+            ropeh[h] = p.rope_cos != nullptr;
           } else {
-            dst = static_cast<T*>(p.v_cache) + cb + (int64_t)(head - p.n_q_heads - p.n_kv_heads) * p.cache_head_stride +
-                  (int64_t)pos * 128;
-            rope = false;
+            dsth[h] = static_cast<T*>(p.v_cache) + cb +
+                      (int64_t)(head - p.n_q_heads - p.n_kv_heads) * p.cache_head_stride + (int64_t)qpos * 128;
           }
+        }
+        float b[32];
 #pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < 2; ++c) {
+          // this row's 32 table entries of dimension chunk c (chunk 0 was
+          // fetched before the accumulator wait), for both heads
+          if (c == 1 && p.rope_cos && qrow_ok) load_rope32(p.rope_cos, p.rope_sin, qpos, 1, rcos, rsin);
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            if (!dsth[h]) break;
             acc_ld(h * 128 + c * 32, v);       // d in [32c, 32c+32)
             acc_ld(h * 128 + 64 + c * 32, b);  // d + 64
-            // this row's 32 table entries, as 16-byte vectors (tables are
-            // 16-byte aligned and rows are 256 bytes)
-            float cs[32], sn[32];
-            if (rope && row_ok) {
-              const float4* cp = reinterpret_cast<const float4*>(p.rope_cos + (int64_t)pos * 64 + c * 32);
-              const float4* sp = reinterpret_cast<const float4*>(p.rope_sin + (int64_t)pos * 64 + c * 32);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 a4 = __ldg(cp + j), b4 = __ldg(sp + j);
-                cs[4 * j] = a4.x; cs[4 * j + 1] = a4.y; cs[4 * j + 2] = a4.z; cs[4 * j + 3] = a4.w;
-                sn[4 * j] = b4.x; sn[4 * j + 1] = b4.y; sn[4 * j + 2] = b4.z; sn[4 * j + 3] = b4.w;
-              }
-            }
+            const bool rope = ropeh[h] && qrow_ok;
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               float x0 = round_to<T>(v[i]), x1 = round_to<T>(b[i]);
-              if (rope && row_ok) {
-                const float y0 = x0 * cs[i] - x1 * sn[i];
-                const float y1 = x0 * sn[i] + x1 * cs[i];
+              if (rope) {
+                const float y0 = x0 * rcos[i] - x1 * rsin[i];
+                const float y1 = x0 * rsin[i] + x1 * rcos[i];
                 x0 = y0;
                 x1 = y1;
               }
               v[i] = x0;
               b[i] = x1;
             }
-            if (row_ok) {
-              store_row32<T>(dst, c * 32, 128, v);
-              store_row32<T>(dst, 64 + c * 32, 128, b);
+            if (qrow_ok) {
+              store_row32<T>(dsth[h], c * 32, 128, v);
+              store_row32<T>(dsth[h], 64 + c * 32, 128, b);
             }
           }
         }
