@@ -464,7 +464,7 @@ cudaError_t launch_decode_attention(const FdParams& p, int n_kv_heads, int R, cu
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   const char* env = getenv("IE_PDL");
-  cfg.numAttrs = (env && env[0] == '0') ? 1 : 2;
+  cfg.numAttrs = ((env && env[0] == '0') || R > pdl_max_rows()) ? 1 : 2;
   return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 

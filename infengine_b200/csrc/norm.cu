@@ -142,7 +142,9 @@ cudaError_t launch(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_launch_enabled() ? 1 : 0;
+  // grid.x is the row count of RMSNorm and the embedding (1 for the step's
+  // bookkeeping kernel)
+  cfg.numAttrs = (pdl_launch_enabled() && (int)grid.x <= pdl_max_rows()) ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 

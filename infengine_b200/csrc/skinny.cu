@@ -722,7 +722,7 @@ static bool pdl_enabled() {
 }
 
 template <typename K, typename... Args>
-static cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, cudaStream_t st, int cluster, Args... args) {
+static cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, cudaStream_t st, int cluster, bool pdl, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -730,7 +730,7 @@ static cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, cudaStream_t st, 
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   int n = 0;
-  if (pdl_enabled()) {
+  if (pdl && pdl_enabled()) {
     attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[n].val.programmaticStreamSerializationAllowed = 1;
     ++n;
@@ -802,7 +802,7 @@ static cudaError_t launch_variant(const SkinnyParams& p, cudaStream_t st) {
   static const int resident = resident_ctas(kernel);
   grid = p.tiles < resident ? p.tiles : resident;
 #endif
-  return launch_pdl(kernel, dim3(grid), dim3(kThreads), st, p.ksplit, p);
+  return launch_pdl(kernel, dim3(grid), dim3(kThreads), st, p.ksplit, p.M <= pdl_max_rows(), p);
 }
 
 template <typename T, int EPI>
