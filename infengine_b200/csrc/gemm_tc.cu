@@ -239,6 +239,9 @@ __device__ __forceinline__ void b_source(const TcArgs& a, int nb, int h, int& ma
   } else {
     map = 0;
     row = nb * BN + h * 128;
+    // a half that lies wholly past the last weight row (N within 128 of the
+    // last tile's start) reloads the first half: those columns are not stored
+    if (row >= a.p.N) row = nb * BN;
   }
 }
 

@@ -30,6 +30,8 @@ def _device_status_clean(ie, cuda):
     (300, 1000, 520),     # ragged M, N (not a multiple of 256) and K (not of 64)
     (2048, 4096, 4096),   # O projection
     (2048, 4096, 14336),  # down projection
+    (1024, 4000, 1024),   # ragged last tile
+    (1536, 800, 256),     # the last tile's second half lies wholly past N
 ])
 def test_gemm_tensor_core(ie, cuda, dt, M, N, K):
     d = oracle.seeded_inputs(M + 7 * N + K, {"x": (M, K), "w": (N, K)}, dt)
