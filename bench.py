@@ -454,14 +454,62 @@ def cpu_baseline(seed: int):
         return min(ts)
 
     t_layer = best(one_layer)
-    del layer
+
+    # the same golden per BASELINE config 1-4, each shape timed on its own
+    # (best of 2): C1 the 4096x4096 GEMV, C2 the FFN block at M = 1/4/8, C3
+    # the four prefill projections at M = 2048 (QKV with RoPE), C4 lm_head +
+    # the reference's argmax at B = 1/8/64
+    def xs(m):
+        return oracle.round_dt(rng.standard_normal((m, H), dtype=np.float32), "bf16")
+
+    def entry(t, nbytes=None, flops=None):
+        e = {"ms": round(t * 1e3, 2)}
+        if nbytes:
+            e["gbs"] = round(nbytes / t / 1e9, 2)
+        if flops:
+            e["gflops"] = round(flops / t / 1e9, 1)
+        return e
+
+    configs = {"c1_gemv_4096x4096": entry(best(lambda: oracle.gemm_cpu(x, layer["wo"], "bf16"), 2), 2 * H * H)}
+    c2 = {}
+    for m in (1, 4, 8):
+        xm = xs(m)
+        c2[f"m{m}"] = entry(best(lambda: oracle.ffn_cpu(xm, layer["wg"], layer["wu"], layer["wd"], "bf16"), 2),
+                            2 * 3 * F * H)
+    configs["c2_ffn_decode"] = c2
+    # C3 on a bounded sample: rows 0..255 of the 2048-token prefill, the
+    # time scaled by 2048 / 256 (the golden is row-independent)
+    rows, scale = 256, 2048 // 256
+    xp = xs(rows)
+    hp = oracle.round_dt(rng.standard_normal((rows, F), dtype=np.float32), "bf16")
+
+    def c3(fn, flops):
+        return entry(best(fn, 2) * scale, flops=flops)
+    configs["c3_prefill_m2048"] = {
+        "qkv_6144x4096": c3(lambda: oracle.qkv_cpu(xp, layer["wq"], layer["wk"], layer["wv"], "bf16", 0, cos, sin),
+                            2 * 2048 * 6144 * H),
+        "o_4096x4096": c3(lambda: oracle.gemm_cpu(xp, layer["wo"], "bf16"), 2 * 2048 * H * H),
+        "gate_up_2x14336x4096": c3(lambda: oracle.swiglu(oracle.gemm_cpu(xp, layer["wg"], "bf16"),
+                                                         oracle.gemm_cpu(xp, layer["wu"], "bf16"), "bf16"),
+                                   2 * 2048 * 2 * F * H),
+        "down_4096x14336": c3(lambda: oracle.gemm_cpu(hp, layer["wd"], "bf16"), 2 * 2048 * H * F),
+        "sample": f"rows 0-{rows - 1} of 2048, time x {scale}",
+    }
+    del layer, xp, hp
     lm = w(V, H)
     t_lm = best(lambda: oracle.lm_head_argmax_cpu(x, lm, "bf16"))
+    c4 = {"b1": entry(t_lm, 2 * V * H)}
+    for B in (8, 64):
+        xb = xs(B)
+        c4[f"b{B}"] = entry(best(lambda: oracle.lm_head_argmax_cpu(xb, lm, "bf16"), 2), 2 * V * H)
+    configs["c4_lm_head_argmax"] = c4
     t_tok = L * t_layer + t_lm
     return {"value": round(1.0 / t_tok, 4), "unit": "tok/s", "cores": cores, "kind": "port",
             "sample": f"1 decoder layer (QKV+RoPE, O, FFN) best of 3 = {t_layer * 1e3:.1f} ms and lm_head+argmax "
                       f"best of 3 = {t_lm * 1e3:.1f} ms, fp32 numpy BLAS on bf16-valued weights, scaled to "
-                      f"{L} layers + lm_head per token"}
+                      f"{L} layers + lm_head per token; `configs` times the same golden at BASELINE configs 1-4 "
+                      f"shape by shape (best of 2; C3 on 256 of the 2048 rows, scaled; gbs counts bf16 weight bytes)",
+            "configs": configs}
 
 
 # --------------------------------------------------------- single-kernel cases
