@@ -233,7 +233,8 @@ int ie_qkv_batched(ie_dtype dt, int B, int H, int n_q_heads, int n_kv_heads, int
  * the reference's roundings. Limits: head_dim 128; n_q_heads a multiple of
  * n_kv_heads; pos0 + S <= INT_MAX and within cache_head_stride / 128 rows.
  * S <= 16 runs the decode kernel below, so its limits apply (group
- * n_q_heads / n_kv_heads in {1, 2, 4, 8}, (pos0 + S) * group <= ~270k).
+ * n_q_heads / n_kv_heads in {1, 2, 4, 8}, (pos0 + S) * group <= ~270k, q
+ * 16-byte aligned with q_head_stride a multiple of 8).
  * Longer chunks run the tensor-core kernel, which streams scores and needs
  * only ceil(S / 128) <= 65535 and n_q_heads <= 65535. A limit that is not met
  * returns IE_ERR_UNSUPPORTED (or IE_ERR_INVALID_ARG for a too-small cache). */
@@ -244,8 +245,8 @@ int ie_attention(ie_dtype dt, int S, int pos0, int n_q_heads, int n_kv_heads, in
 
 /* Decode-time attention (same chain as ie_attention) for R query rows that
  * each read their whole cache, split over the GPU: every (row, KV head) is
- * served by a cluster of 8 CTAs, each over 1/8 of the cache rows, merged
- * through distributed shared memory. Row m belongs to sequence
+ * served by a cluster of 8 CTAs (16 for at most 4 KV heads), each over an
+ * equal share of the cache rows, merged through distributed shared memory. Row m belongs to sequence
  * m / rows_per_seq (cache at + that * cache_batch_stride elements) and sits at
  * position positions[m] (device array, R entries; read when the kernel runs,
  * so a captured graph follows it) or, when positions is NULL, pos0 + m; it
@@ -253,7 +254,8 @@ int ie_attention(ie_dtype dt, int S, int pos0, int n_q_heads, int n_kv_heads, in
  * q_head_stride), out [R][n_q_heads*128] (row stride ld_out). A position
  * outside [0, cache_rows) writes zeros and sets IE_ERR_INVALID_ARG in
  * ie_device_status. n_q_heads / n_kv_heads in {1, 2, 4, 8}; cache_rows *
- * group <= ~270k. The reference has no batched or device-positioned form of
+ * group <= ~270k. q, k_cache and v_cache 16-byte aligned, q_head_stride and
+ * the cache strides multiples of 8 (IE_ERR_ALIGNMENT otherwise). The reference has no batched or device-positioned form of
  * this (decode_attn, kernels/attn.cu:390-439, serves one row). */
 int ie_attention_decode(ie_dtype dt, int R, int rows_per_seq, int n_q_heads, int n_kv_heads, int head_dim,
                         const void* q, int64_t q_head_stride,

@@ -34,37 +34,40 @@
 // over the GPU: one thread-block cluster of C CTAs per (query row, KV head),
 // C = 16 for at most 4 KV heads, else 8, whatever the number of rows (so a
 // row's result does not depend on the batch); CTA c of the cluster takes
-// cache rows [c*len/C, (c+1)*len/C).
+// cache rows [c*len/C, (c+1)*len/C). A CTA is 4 warps.
 //  * Cache rows reach shared memory by untiled bulk copies
-//    (cp.async.bulk, 64 rows = 16 KB each) through a 6-deep ring completed on
-//    mbarriers, so a CTA keeps up to 96 KB of K/V in flight. Rows older than
-//    the launch's first query row are requested before the kernel waits for
-//    its predecessor (programmatic launch), so their latency overlaps the
-//    QKV projection's tail.
+//    (cp.async.bulk, 64 rows = 16 KB each) through a ring of 2-6 slots
+//    completed on mbarriers. Rows older than the launch's first query row are
+//    requested before the kernel waits for its predecessor (programmatic
+//    launch), so their latency overlaps the QKV projection's tail.
 //  * Scores run on the tensor cores (m16n8k16: 16 cache rows x the group's
-//    query heads, padded to 8, per instruction), the A operand read straight
-//    from the copied rows, q held in B fragments.
+//    query heads, padded to 8): warp w takes rows 16w..16w+15 of a chunk, the
+//    two 64-dimension halves in two accumulators added low + high, then
+//    rounded, scaled and rounded; the row maximum is kept in registers.
 //  * The softmax keeps the reference's chain (scores rounded, scaled and
 //    rounded; e = exp(t - max) summed in fp32 and stored rounded;
 //    p = round(round(e) * (1/sum))): the row maximum and the sum are exact
-//    cluster-wide values, exchanged through distributed shared memory in a
-//    fixed rank order, so no rescaling of partial results is involved.
-//  * p.V partials ([group][128] fp32 per CTA) are summed across the cluster in
-//    rank order; each CTA rounds and stores 1/8 of the row's outputs.
+//    cluster-wide values. Each CTA pushes its maximum, its sum and its p.V
+//    partial into every peer's shared memory (st.async, completing on the
+//    peer's mbarrier), and sums what it receives in rank order.
+//  * p.V runs on the tensor cores too: P (heads x 16 cache rows) is the A
+//    operand, V the B operand, its pairs of rows packed by byte permutes from
+//    8-byte shared-memory loads; warp w owns output dimensions 32w..32w+31
+//    for the whole slice, so no cross-warp sum is needed. CTA r rounds and
+//    stores the r-th 1/C of the row's outputs.
 // Results are deterministic. Every mbarrier wait is bounded (2 s unless
-// ie_set_wait_limit_ns says otherwise): on expiry
-// IE_ERR_TIMEOUT is recorded, no further copies are issued, the outstanding
-// ones are waited for (bounded) before the CTA exits, and the cluster
-// barriers are still passed by every CTA.
+// ie_set_wait_limit_ns says otherwise): on expiry IE_ERR_TIMEOUT is recorded,
+// no further copies are issued, and before the CTA exits the outstanding
+// copies and the peers' pushes into it are waited for (bounded).
 namespace ie {
 
 __device__ int g_attn_status = 0;
-// limit of one bulk-copy wait (ie_set_wait_limit_ns)
+// limit of one bulk-copy or exchange wait (ie_set_wait_limit_ns)
 __device__ unsigned long long g_attn_wait_ns = kDefaultWaitNs;
 
 namespace {
 
-constexpr int kFdThreads = 256;
+constexpr int kFdThreads = 128;
 constexpr int kFdWarps = kFdThreads / 32;
 constexpr int kFdRows = 64;
 constexpr int kFdStages = 6;  // deepest ring (the size limits are checked against it)
@@ -82,9 +85,17 @@ struct FdParams {
   int pos0, rows_per_seq;
   void* out;
   int64_t ld_out;
-  int cap;     // score slots per head in shared memory (>= ceil(cache_rows / 8))
+  int cap;     // score slots per head in shared memory (fd_score_cap)
   int stages;  // ring depth in 64-row chunks, 2 .. kFdStages (occupancy only; no effect on the results)
+  int early;   // launched to overlap its predecessor: the older rows are requested before waiting for it
 };
+
+// Score slots per head: at least the longest slice rounded up to whole
+// 16-row MMA steps (an 8-CTA slice of cache_rows rows); kept 16 above a
+// multiple of 64 so that the heads' rows of P start in different banks.
+__host__ __device__ constexpr int fd_score_cap(int cache_rows) {
+  return ((cache_rows + 7) / 8 + 63) / 64 * 64 + 16;
+}
 
 __device__ __forceinline__ uint32_t fd_smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -95,6 +106,18 @@ __device__ __forceinline__ bool fd_try(uint32_t bar, uint32_t parity) {
       "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// the same test with acquire at cluster scope: the exchange barriers are
+// completed by the peers' st.async
+__device__ __forceinline__ bool fd_try_cluster(uint32_t bar) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\nmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\nselp.u32 %0, 1, 0, "
+      "p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar)
       : "memory");
   return ok != 0;
 }
@@ -118,21 +141,35 @@ __device__ __forceinline__ bool fd_wait(uint32_t bar, uint32_t parity, volatile 
   }
   return true;
 }
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// The same shared-memory word of every CTA of the cluster (rank order). The
-// loads carry no memory clobber: they follow a cluster barrier and are all
-// issued before any is used.
-template <int C>
-__device__ __forceinline__ void ld_cluster_all(const float* local, float (&v)[C]) {
-  const uint32_t a = fd_smem_u32(local);
-#pragma unroll
-  for (unsigned r = 0; r < C; ++r) {
-    uint32_t remote;
-    asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(a), "r"(r));
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v[r]) : "r"(remote));
+// Bounded wait for one exchange (single phase per launch).
+__device__ __forceinline__ void fd_wait_exchange(uint32_t bar, volatile int* abort_s, unsigned long long limit) {
+  if (fd_try_cluster(bar)) return;
+  const unsigned long long t0 = fd_now();
+  while (!fd_try_cluster(bar)) {
+    if (fd_now() - t0 > limit) {
+      atomicExch(&g_attn_status, IE_ERR_TIMEOUT);
+      *abort_s = 1;
+      return;
+    }
   }
+}
+__device__ __forceinline__ uint32_t fd_peer(uint32_t local, unsigned rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(rank));
+  return remote;
+}
+// 4 bytes into a peer's shared memory, counted on the peer's mbarrier
+__device__ __forceinline__ void fd_push(uint32_t raddr, float v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr),
+               "r"(__float_as_uint(v)), "r"(rbar)
+               : "memory");
+}
+__device__ __forceinline__ void fd_push4(uint32_t raddr, float a, float b, float c, float d, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   raddr),
+               "r"(__float_as_uint(a)), "r"(__float_as_uint(b)), "r"(__float_as_uint(c)), "r"(__float_as_uint(d)),
+               "r"(rbar)
+               : "memory");
 }
 
 // m16n8k16 tensor-core product, fp32 accumulation (A and B of the same type).
@@ -150,27 +187,25 @@ __device__ __forceinline__ void fd_mma(float (&c)[4], uint32_t a0, uint32_t a1, 
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-template <typename T>
-__device__ __forceinline__ uint32_t fd_pack2(float lo, float hi) {
-  T a = DT<T>::from_f(lo), b = DT<T>::from_f(hi);
-  return (uint32_t)(*reinterpret_cast<uint16_t*>(&a)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&b)) << 16);
-}
 
 template <typename T, int G, int C>
 __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdParams p) {
+  constexpr int kPer = G * 128 / C;  // outputs each CTA of the cluster reduces and stores
+  static_assert(kPer % 8 == 0 && kPer <= kFdThreads, "output slice per CTA");
   extern __shared__ __align__(128) unsigned char fd_smem[];
-  __shared__ float qf[G][128];
-  __shared__ float opart[G * 128];
-  __shared__ float red[kFdWarps][G];
-  __shared__ float spart[2][kFdRows][G];  // half-dimension partial scores of a chunk
-  __shared__ float cmax[G], csum[G], gmax[G], ginv[G];
+  __shared__ __align__(16) float xout[C * kPer];  // [source rank][kPer] p.V partials pushed by the cluster
+  __shared__ float xmax[C][G], xsum[C][G];         // [source rank][head] maxima and sums pushed by the cluster
+  __shared__ float wred[kFdWarps][G];
+  __shared__ float gmax[G], ginv[G];
   __shared__ __align__(8) unsigned long long bars[kFdStages];
+  __shared__ __align__(8) unsigned long long xbar[3];  // maxima, sums, partials
   __shared__ int abort_s, fail_at;
 
   T* ring = reinterpret_cast<T*>(fd_smem);
   const int S = p.stages;
-  T* sc = reinterpret_cast<T*>(fd_smem + S * kFdStageBytes);
+  T* sc = reinterpret_cast<T*>(fd_smem + S * kFdStageBytes);  // [G][cap]: scores, then e, then p
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int fg = lane >> 2, ft = lane & 3;
   unsigned rank;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
   const int hk = blockIdx.y, m = blockIdx.z;
@@ -226,43 +261,55 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
     copy(i, 0, INT_MAX);
   };
 
+  // B fragments of q for the score MMAs, from global memory: lane (g, t)
+  // holds, for each half hf and 32-dimension k-step ks, the 8 dimensions
+  // 64 hf + 32 ks + 8t .. +7 of head g (zero for g >= G) as one 16-byte load,
+  // in the order the A fragments use (MMA j takes elements 4j .. 4j+3 of a
+  // lane's 8-dimension load). Without a predecessor to overlap, q is read
+  // before the cache copies fill the memory system; otherwise after the wait
+  // (the predecessor writes it).
+  uint4 qf[2][2];
+  auto load_q = [&] {
+    const uint4* qv = reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) +
+                                                     (int64_t)(hk * G + (fg < G ? fg : 0)) * p.q_head_stride +
+                                                     (int64_t)m * 128);
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) qf[hf][ks] = fg < G ? qv[8 * hf + 4 * ks + ft] : make_uint4(0u, 0u, 0u, 0u);
+  };
+  if (!p.early) load_q();
+
   const int first = min(S, total);
   if (tid == 0) {
     for (int s = 0; s < S; ++s)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(fd_smem_u32(&bars[s])) : "memory");
+    // each exchange completes when all C peers' bytes have landed
+    const uint32_t xbytes[3] = {C * G * 4u, C * G * 4u, C * kPer * 4u};
+    for (int k = 0; k < 3; ++k) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(fd_smem_u32(&xbar[k])) : "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(fd_smem_u32(&xbar[k])),
+                   "r"(xbytes[k])
+                   : "memory");
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     abort_s = 0;
     fail_at = INT_MAX;
     for (int i = 0; i < first; ++i) {
       arm(i);
-      copy(i, 0, first_new);
+      if (p.early) copy(i, 0, first_new);
     }
   }
+  __syncwarp();
+  // every peer's exchange barriers are initialised before the first push:
+  // arrive now, wait right before pushing
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (p.early) load_q();
   if (tid == 0)
-    for (int i = 0; i < first; ++i) copy(i, first_new, INT_MAX);
-  __syncthreads();
-
-  for (int i = tid; i < G * 128; i += kFdThreads) {
-    const int h = i >> 7, d = i & 127;
-    qf[h][d] = DT<T>::to_f(static_cast<const T*>(p.q)[(int64_t)(hk * G + h) * p.q_head_stride + (int64_t)m * 128 + d]);
-  }
-  __syncthreads();
-  // B fragments of q for the score MMAs. Warp w multiplies the 16-row tile
-  // w & 3 of a chunk over head dimensions [64 (w >> 2), +64); lane (g, t)
-  // holds, for each 32-dimension k-step, the 8 dimensions 8t .. 8t+7 of head g
-  // (zero for g >= G) in the order its A chunks use (the same k permutation as
-  // the decode GEMV: MMA j takes elements 4j .. 4j+3 of the chunk).
-  const int fg = lane >> 2, ft = lane & 3, tile_w = warp & 3, half_w = warp >> 2;
-  uint32_t qb[2][4];
-#pragma unroll
-  for (int ks = 0; ks < 2; ++ks)
-#pragma unroll
-    for (int e2 = 0; e2 < 4; ++e2) {
-      const int d = 64 * half_w + 32 * ks + 8 * ft + 2 * e2;
-      qb[ks][e2] = fg < G ? fd_pack2<T>(qf[fg][d], qf[fg][d + 1]) : 0u;
-    }
+    for (int i = 0; i < first; ++i) copy(i, p.early ? first_new : 0, INT_MAX);
+  __syncthreads();  // abort_s, fail_at
 
   auto wait_chunk = [&](int i) {
     if (!fd_wait(fd_smem_u32(&bars[i % S]), (uint32_t)((i / S) & 1), &abort_s))
@@ -273,133 +320,174 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
     if (tid == 0 && !abort_s && i + S < total) issue(i + S);
   };
 
-  // ---- scores on the tensor cores: S[row][head] = K[row] . q[head], one
-  // m16n8k16 per 16 dimensions; the two dimension halves of a tile meet in
-  // shared memory (low half + high half), then round, scale, round
+  // ---- scores: S[row][head] = K[row] . q[head] over the low and the high
+  // 64 dimensions (4 MMAs each), added low + high, then rounded, scaled by
+  // rsqrt(128) and rounded; lane (g, t) gets rows g, g + 8 of its warp's tile
+  // and heads 2t, 2t + 1
   const float scale = rsqrtf(128.0f);
+  float mx[2] = {-INFINITY, -INFINITY};
   for (int i = 0; i < nk; ++i) {
     wait_chunk(i);
     const T* tile = ring + (i % S) * kFdRows * 128;
     const int r0 = i * kFdRows, rows = min(kFdRows, n - r0);
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-    const T* ra = tile + (tile_w * 16 + fg) * 128 + 64 * half_w + 8 * ft;
+    if (16 * warp < rows) {
+      float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-    for (int ks = 0; ks < 2; ++ks) {
-      const uint4 wa = *reinterpret_cast<const uint4*>(ra + 32 * ks);            // row g
-      const uint4 wb = *reinterpret_cast<const uint4*>(ra + 8 * 128 + 32 * ks);  // row g + 8
-      fd_mma<T>(c, wa.x, wb.x, wa.y, wb.y, qb[ks][0], qb[ks][1]);
-      fd_mma<T>(c, wa.z, wb.z, wa.w, wb.w, qb[ks][2], qb[ks][3]);
-    }
-    // c: rows g, g + 8 of the tile x heads 2t, 2t + 1
-    const int rr = tile_w * 16 + fg;
-    if (2 * ft < G) {
-      spart[half_w][rr][2 * ft] = c[0];
-      spart[half_w][rr + 8][2 * ft] = c[2];
-    }
-    if (2 * ft + 1 < G) {
-      spart[half_w][rr][2 * ft + 1] = c[1];
-      spart[half_w][rr + 8][2 * ft + 1] = c[3];
-    }
-    __syncthreads();
-    for (int idx = tid; idx < rows * G; idx += kFdThreads) {
-      const int r = idx / G, h = idx - r * G;
-      const float v = spart[0][r][h] + spart[1][r][h];
-      sc[h * p.cap + r0 + r] = DT<T>::from_f(round_to<T>(round_to<T>(v) * scale));
+      for (int hf = 0; hf < 2; ++hf) {
+        const T* ra = tile + (16 * warp + fg) * 128 + 64 * hf + 8 * ft;
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          const uint4 wa = *reinterpret_cast<const uint4*>(ra + 32 * ks);            // row g
+          const uint4 wb = *reinterpret_cast<const uint4*>(ra + 8 * 128 + 32 * ks);  // row g + 8
+          fd_mma<T>(c[hf], wa.x, wb.x, wa.y, wb.y, qf[hf][ks].x, qf[hf][ks].y);
+          fd_mma<T>(c[hf], wa.z, wb.z, wa.w, wb.w, qf[hf][ks].z, qf[hf][ks].w);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int row = 16 * warp + fg + 8 * (k >> 1), h = 2 * ft + (k & 1);
+        if (h < G && row < rows) {
+          const float s = round_to<T>(round_to<T>(c[0][k] + c[1][k]) * scale);
+          sc[h * p.cap + r0 + row] = DT<T>::from_f(s);
+          mx[k & 1] = fmaxf(mx[k & 1], s);
+        }
+      }
     }
     next(i);
   }
 
   // ---- softmax with cluster-wide max and sum
-  float mx[G];
 #pragma unroll
-  for (int h = 0; h < G; ++h) mx[h] = -INFINITY;
-  for (int j = tid; j < n; j += kFdThreads)
+  for (int e = 0; e < 2; ++e) {
 #pragma unroll
-    for (int h = 0; h < G; ++h) mx[h] = fmaxf(mx[h], DT<T>::to_f(sc[h * p.cap + j]));
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], off));
-    if (lane == 0) red[warp][h] = mx[h];
+    for (int off = 4; off < 32; off <<= 1) mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], off));
+    if (fg == 0 && 2 * ft + e < G) wred[warp][2 * ft + e] = mx[e];
   }
   __syncthreads();
-  if (tid < G) {
-    float v = -INFINITY;
-    for (int w = 0; w < kFdWarps; ++w) v = fmaxf(v, red[w][tid]);
-    cmax[tid] = v;
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (tid < C * G) {  // this CTA's maximum of head h to rank r
+    const int h = tid % G, r = tid / G;
+    float v = wred[0][h];
+#pragma unroll
+    for (int w = 1; w < kFdWarps; ++w) v = fmaxf(v, wred[w][h]);
+    fd_push(fd_peer(fd_smem_u32(&xmax[rank][h]), r), v, fd_peer(fd_smem_u32(&xbar[0]), r));
   }
-  cluster_sync_all();
+  const unsigned long long xlimit = g_attn_wait_ns;
+  fd_wait_exchange(fd_smem_u32(&xbar[0]), &abort_s, xlimit);
   if (tid < G) {
-    float v = -INFINITY;
-    float all[C];
-    ld_cluster_all<C>(&cmax[tid], all);
-    for (unsigned r = 0; r < C; ++r) v = fmaxf(v, all[r]);
+    float v = xmax[0][tid];
+#pragma unroll
+    for (int r = 1; r < C; ++r) v = fmaxf(v, xmax[r][tid]);
     gmax[tid] = v;
   }
   __syncthreads();
+  // e = exp(t - max), stored rounded, in blocks of 8 slots per thread (head
+  // h, slots 8b .. 8b+7); slots from n up to the next 16-row step get 0. A
+  // thread adds its slots in order, then its blocks in order.
+  const int n16 = (n + 15) & ~15, nb = n16 / 8;
   float sm[G];
 #pragma unroll
   for (int h = 0; h < G; ++h) sm[h] = 0.f;
-  for (int j = tid; j < n; j += kFdThreads)
+  for (int v = tid; v < G * nb; v += kFdThreads) {
+    const int h = v / nb, j = (v - h * nb) * 8;
+    uint4* blk = reinterpret_cast<uint4*>(sc + h * p.cap + j);
+    uint4 raw = *blk;
+    T* x = reinterpret_cast<T*>(&raw);
+    const float g = gmax[h];
+    float s8 = 0.f;
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const float e = expf(DT<T>::to_f(sc[h * p.cap + j]) - gmax[h]);
-      sm[h] += e;
-      sc[h * p.cap + j] = DT<T>::from_f(e);
+    for (int k = 0; k < 8; ++k) {
+      const float e = j + k < n ? expf(DT<T>::to_f(x[k]) - g) : 0.f;
+      s8 += e;
+      x[k] = DT<T>::from_f(e);
     }
+    *blk = raw;
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh)
+      if (hh == h) sm[hh] += s8;
+  }
 #pragma unroll
   for (int h = 0; h < G; ++h) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) sm[h] += __shfl_xor_sync(0xffffffffu, sm[h], off);
   }
-  __syncthreads();  // red is reused
   if (lane == 0)
 #pragma unroll
-    for (int h = 0; h < G; ++h) red[warp][h] = sm[h];
+    for (int h = 0; h < G; ++h) wred[warp][h] = sm[h];
   __syncthreads();
-  if (tid < G) {
-    float v = 0.f;
-    for (int w = 0; w < kFdWarps; ++w) v += red[w][tid];
-    csum[tid] = v;
+  if (tid < C * G) {  // this CTA's sum of head h (warps in order) to rank r
+    const int h = tid % G, r = tid / G;
+    float v = wred[0][h];
+#pragma unroll
+    for (int w = 1; w < kFdWarps; ++w) v += wred[w][h];
+    fd_push(fd_peer(fd_smem_u32(&xsum[rank][h]), r), v, fd_peer(fd_smem_u32(&xbar[1]), r));
   }
-  cluster_sync_all();
+  fd_wait_exchange(fd_smem_u32(&xbar[1]), &abort_s, xlimit);
   if (tid < G) {
-    float v = 0.f;
-    float all[C];
-    ld_cluster_all<C>(&csum[tid], all);
-    for (unsigned r = 0; r < C; ++r) v += all[r];
+    float v = xsum[0][tid];
+#pragma unroll
+    for (int r = 1; r < C; ++r) v += xsum[r][tid];
     ginv[tid] = 1.0f / v;
   }
   __syncthreads();
-  for (int j = tid; j < n; j += kFdThreads)
+  // p = round(round(e) / sum) (the zero slots stay zero)
+  for (int v = tid; v < G * nb; v += kFdThreads) {
+    const int h = v / nb, j = (v - h * nb) * 8;
+    uint4* blk = reinterpret_cast<uint4*>(sc + h * p.cap + j);
+    uint4 raw = *blk;
+    T* x = reinterpret_cast<T*>(&raw);
+    const float iv = ginv[h];
 #pragma unroll
-    for (int h = 0; h < G; ++h) sc[h * p.cap + j] = DT<T>::from_f(DT<T>::to_f(sc[h * p.cap + j]) * ginv[h]);
+    for (int k = 0; k < 8; ++k) x[k] = DT<T>::from_f(DT<T>::to_f(x[k]) * iv);
+    *blk = raw;
+  }
   __syncthreads();
 
-  // ---- p.V: warp per cache row, lane per 4 dims
-  float acc[G][4];
+  // ---- p.V on the tensor cores: out[head][dim] += P[head][row] V[row][dim]
+  // per 16-row step. A = P (rows g of lane (g, t) = head g, zero from G on),
+  // B = V: lane (g, t) loads dimensions 32w + 4g .. +3 of rows 2t, 2t+1,
+  // 2t+8, 2t+9 and packs the row pairs of each dimension; the MMA of
+  // dimension offset d (0..3) then holds, in its column n, dimension
+  // 32w + 4n + d.
+  float acc[4][4];
 #pragma unroll
-  for (int h = 0; h < G; ++h)
+  for (int d = 0; d < 4; ++d)
 #pragma unroll
-    for (int d = 0; d < 4; ++d) acc[h][d] = 0.f;
+    for (int e = 0; e < 4; ++e) acc[d][e] = 0.f;
+  // one 16-row step; rows past the slice hold stale data and are read as
+  // zero (their p is zero too)
+  auto pv_step = [&](const T* tile, int r0, int k0, int rows, bool full) {
+    const int kr = k0 + 2 * ft;
+    uint32_t a0 = 0u, a2 = 0u;
+    if (fg < G) {
+      const T* pr = sc + fg * p.cap + r0 + kr;
+      a0 = *reinterpret_cast<const uint32_t*>(pr);
+      a2 = *reinterpret_cast<const uint32_t*>(pr + 8);
+    }
+    const T* vr = tile + kr * 128 + 32 * warp + 4 * fg;
+    const uint2 z = make_uint2(0u, 0u);
+    const uint2 va = full || kr < rows ? *reinterpret_cast<const uint2*>(vr) : z;
+    const uint2 vb = full || kr + 1 < rows ? *reinterpret_cast<const uint2*>(vr + 128) : z;
+    const uint2 vc = full || kr + 8 < rows ? *reinterpret_cast<const uint2*>(vr + 8 * 128) : z;
+    const uint2 vd = full || kr + 9 < rows ? *reinterpret_cast<const uint2*>(vr + 9 * 128) : z;
+    fd_mma<T>(acc[0], a0, 0u, a2, 0u, __byte_perm(va.x, vb.x, 0x5410), __byte_perm(vc.x, vd.x, 0x5410));
+    fd_mma<T>(acc[1], a0, 0u, a2, 0u, __byte_perm(va.x, vb.x, 0x7632), __byte_perm(vc.x, vd.x, 0x7632));
+    fd_mma<T>(acc[2], a0, 0u, a2, 0u, __byte_perm(va.y, vb.y, 0x5410), __byte_perm(vc.y, vd.y, 0x5410));
+    fd_mma<T>(acc[3], a0, 0u, a2, 0u, __byte_perm(va.y, vb.y, 0x7632), __byte_perm(vc.y, vd.y, 0x7632));
+  };
   for (int i = nk; i < total; ++i) {
     wait_chunk(i);
     const T* tile = ring + (i % S) * kFdRows * 128;
     const int r0 = (i - nk) * kFdRows, rows = min(kFdRows, n - r0);
-#pragma unroll 4
-    for (int r = warp; r < rows; r += kFdWarps) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(tile + r * 128 + lane * 4);
-      const T* e = reinterpret_cast<const T*>(&raw);
+    if (rows == kFdRows) {
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float pw = DT<T>::to_f(sc[h * p.cap + r0 + r]);
-#pragma unroll
-        for (int d = 0; d < 4; ++d) acc[h][d] = fmaf(pw, DT<T>::to_f(e[d]), acc[h][d]);
-      }
+      for (int k0 = 0; k0 < kFdRows; k0 += 16) pv_step(tile, r0, k0, rows, true);
+    } else {
+      for (int k0 = 0; k0 < rows; k0 += 16) pv_step(tile, r0, k0, rows, false);
     }
     next(i);
   }
-  // copies a failed wait left in flight finish before the ring is reused
+  // copies a failed wait left in flight finish before the CTA exits
   if (tid == 0 && fail_at < issued) {
     for (int i = fail_at; i < issued; ++i) {
       const unsigned long long t0 = fd_now();
@@ -408,32 +496,30 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
       }
     }
   }
-  __syncthreads();
 
-  // ---- CTA partial (warps summed in order), then the cluster sum in rank order
-  float* part = reinterpret_cast<float*>(fd_smem);  // [warps][G][128], over the drained ring
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-#pragma unroll
-    for (int d = 0; d < 4; ++d) part[(warp * G + h) * 128 + lane * 4 + d] = acc[h][d];
-  __syncthreads();
-  for (int e = tid; e < G * 128; e += kFdThreads) {
-    float s = 0.f;
-    for (int w = 0; w < kFdWarps; ++w) s += part[w * G * 128 + e];
-    opart[e] = s;
+  // ---- the cluster sum of the p.V partials: lane (g, t) of warp w holds head
+  // g, dimensions 32w + 8t .. +7 (acc[d][0] is dimension 8t + d, acc[d][1]
+  // dimension 8t + 4 + d); they go to the CTA that stores them
+  if (fg < G) {
+    const int e = fg * 128 + 32 * warp + 8 * ft;
+    const unsigned owner = (unsigned)(e / kPer);
+    const uint32_t raddr = fd_peer(fd_smem_u32(&xout[rank * kPer + (e - (int)owner * kPer)]), owner);
+    const uint32_t rbar = fd_peer(fd_smem_u32(&xbar[2]), owner);
+    fd_push4(raddr, acc[0][0], acc[1][0], acc[2][0], acc[3][0], rbar);
+    fd_push4(raddr + 16, acc[0][1], acc[1][1], acc[2][1], acc[3][1], rbar);
   }
-  cluster_sync_all();
-  constexpr int kPer = G * 128 / C;
+  fd_wait_exchange(fd_smem_u32(&xbar[2]), &abort_s, xlimit);
   if (tid < kPer) {
+    float s = xout[tid];
+#pragma unroll
+    for (int r = 1; r < C; ++r) s += xout[r * kPer + tid];
     const int e = (int)rank * kPer + tid;
-    float s = 0.f;
-    float all[C];
-    ld_cluster_all<C>(&opart[e], all);
-    for (unsigned r = 0; r < C; ++r) s += all[r];
     const int h = e >> 7, d = e & 127;
     static_cast<T*>(p.out)[(int64_t)m * p.ld_out + (int64_t)(hk * G + h) * 128 + d] = DT<T>::from_f(s);
   }
-  cluster_sync_all();  // remote reads of opart are done before any CTA exits
+  // after a timeout, late pushes from the peers land before this CTA exits
+  if (abort_s)
+    for (int k = 0; k < 3; ++k) fd_wait_exchange(fd_smem_u32(&xbar[k]), &abort_s, kDrainWaitNs);
 }
 
 template <typename T, int G, int C>
@@ -465,16 +551,18 @@ cudaError_t launch_decode_attention(const FdParams& p, int n_kv_heads, int R, cu
   cfg.attrs = attr;
   const char* env = getenv("IE_PDL");
   cfg.numAttrs = ((env && env[0] == '0') || R > pdl_max_rows()) ? 1 : 2;
-  return cudaLaunchKernelEx(&cfg, kernel, p);
+  FdParams pl = p;
+  pl.early = cfg.numAttrs == 2;
+  return cudaLaunchKernelEx(&cfg, kernel, pl);
 }
 
 // Ring depth of a launch: the full 6 stages while the grid fits twice per SM,
 // else the deepest ring that lets every CTA be resident at once (the ring is
-// most of a CTA's shared memory), at least 2 (the CTA partials reuse 32 KB of
-// it). Only residency depends on it: which warp adds which cache row, and so
-// every result bit, comes from the 64-row chunks. IE_FD_STAGES=2..6 in the
-// environment fixes it (for measurements).
-int fd_stages(int ctas, int group, int cap) {
+// most of a CTA's shared memory), at least 2. Only residency depends on it:
+// which MMA adds which cache row, and so every result bit, comes from the
+// 64-row chunks. IE_FD_STAGES=2..6 in the environment fixes it (for
+// measurements).
+int fd_stages(int ctas, int group, int cap, int cluster) {
   static const int forced = [] {
     const char* e = getenv("IE_FD_STAGES");
     const int v = e ? atoi(e) : 0;
@@ -489,11 +577,11 @@ int fd_stages(int ctas, int group, int cap) {
   }();
   const int per_sm = (ctas + sms - 1) / sms;
   if (per_sm <= 2) return kFdStages;
-  // static shared memory of the kernel (q, partials, scores scratch) and a
-  // reserve, against the 227 KB a B200 SM offers
-  const size_t fixed = (size_t)group * 128 * 4 * 2 + (size_t)2 * kFdRows * group * 4 + 2048 + 1024;
+  // static shared memory (exchange buffers, barriers) and the 1 KB the
+  // runtime keeps per CTA, against the 228 KB of a B200 SM
+  const size_t fixed = (size_t)group * 128 * 4 + (size_t)2 * cluster * group * 4 + 512 + 1024;
   for (int s = kFdStages; s > 2; --s)
-    if ((size_t)per_sm * ((size_t)s * kFdStageBytes + (size_t)group * cap * 2 + fixed) <= 227u * 1024u) return s;
+    if ((size_t)per_sm * ((size_t)s * kFdStageBytes + (size_t)group * cap * 2 + fixed) <= 228u * 1024u) return s;
   return 2;
 }
 
@@ -502,9 +590,6 @@ int fd_stages(int ctas, int group, int cap) {
 // The key slices and the order in which their partial sums meet follow from
 // the cluster size, so it must not depend on how many rows share a launch: a
 // row then gets the same bits alone, in a batch, or inside a verify block.
-// Graph-timed at position 2048, 8 -> 16 CTAs: 8 KV heads one row 9.3 -> 8.9 us
-// but 8 rows slower (batch-8 decode 5.18 ms a step with 16, about 4.8 with 8);
-// 1 KV head 8.8 -> 6.9 us; at 8191 23.4 -> 14.4 us.
 // IE_FD_CLUSTER=8|16 in the environment forces one (for measurements).
 int fd_cluster_size(int n_kv_heads) {
   static const int forced = [] {
@@ -548,7 +633,8 @@ extern "C" int ie_attention_decode(ie_dtype dt, int R, int rows_per_seq, int n_q
   if (R == 0) return IE_OK;
   if (!q || !k_cache || !v_cache || !out) return IE_ERR_INVALID_ARG;
   if (R % rows_per_seq || R > 65535 || n_kv_heads > 65535) return IE_ERR_INVALID_ARG;
-  if (!aligned16(k_cache) || !aligned16(v_cache) || (cache_head_stride % 8) || (cache_batch_stride % 8))
+  if (!aligned16(k_cache) || !aligned16(v_cache) || (cache_head_stride % 8) || (cache_batch_stride % 8) ||
+      !aligned16(q) || (q_head_stride % 8))
     return IE_ERR_ALIGNMENT;
   if (ld_out < (int64_t)n_q_heads * 128 || q_head_stride < (int64_t)R * 128) return IE_ERR_INVALID_ARG;
   if (cache_head_stride < (int64_t)cache_rows * 128) return IE_ERR_INVALID_ARG;
@@ -569,9 +655,10 @@ extern "C" int ie_attention_decode(ie_dtype dt, int R, int rows_per_seq, int n_q
   p.ld_out = ld_out;
   const int C = fd_cluster_size(n_kv_heads);
   // score slots per head: the 8-CTA slice bound serves both cluster sizes
-  p.cap = ((cache_rows + 8 - 1) / 8 + 7) / 8 * 8;
+  p.cap = fd_score_cap(cache_rows);
   if (kFdRingBytes + (size_t)group * p.cap * 2 > 200 * 1024) return IE_ERR_UNSUPPORTED;
-  p.stages = fd_stages(C * n_kv_heads * R, group, p.cap);
+  p.stages = fd_stages(C * n_kv_heads * R, group, p.cap, C);
+  p.early = 0;  // set by the launcher
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e;
 #define IE_FD(T, CL)                                                                   \
