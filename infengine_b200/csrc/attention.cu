@@ -109,18 +109,11 @@ __device__ __forceinline__ bool fd_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// the same test with acquire at cluster scope: the exchange barriers are
-// completed by the peers' st.async
-__device__ __forceinline__ bool fd_try_cluster(uint32_t bar) {
-  uint32_t ok;
-  asm volatile(
-      "{\n.reg .pred p;\nmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\nselp.u32 %0, 1, 0, "
-      "p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar)
-      : "memory");
-  return ok != 0;
-}
+// Phase 0 of an exchange barrier, which the peers' st.async complete. The
+// pushed bytes are in this CTA's shared memory once the barrier has counted
+// them, as with the bulk copies, so the default CTA-scope wait suffices (an
+// acquire at cluster scope would add a fence to every poll).
+__device__ __forceinline__ bool fd_try_cluster(uint32_t bar) { return fd_try(bar, 0u); }
 __device__ __forceinline__ unsigned long long fd_now() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -302,8 +295,9 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
   }
   __syncwarp();
   // every peer's exchange barriers are initialised before the first push:
-  // arrive now, wait right before pushing
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  // arrive now (the init fence above orders the initialisation), wait right
+  // before pushing
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (p.early) load_q();
