@@ -134,14 +134,17 @@ def test_attention_rejects_bad_arguments_without_device(ie):
     assert call(ok(pos0=big, S=16, chs=1 << 62)) == -1
     # ie_attention_decode(dt, R, rows_per_seq, nq, nkv, hd, q, q_hs, k, v, chs, cbs, cache_rows, positions,
     #                     pos0, out, ld_out, stream)
-    dec = lambda R=1, rps=1, nq=32, nkv=8, rows=2048, pos0=0, k=f: lib.ie_attention_decode(
-        1, R, rps, nq, nkv, 128, f, 128 * max(R, 1), k, f, chs, 0, rows, None, pos0, f, 4096, None)
+    dec = lambda R=1, rps=1, nq=32, nkv=8, rows=2048, pos0=0, k=f, q=f, qhs=None: lib.ie_attention_decode(
+        1, R, rps, nq, nkv, 128, q, qhs if qhs is not None else 128 * max(R, 1), k, f, chs, 0, rows, None, pos0, f,
+        4096, None)
     assert dec(nq=24) == -3                            # group of 3 query heads per KV head
     assert dec(R=3, rps=2) == -1                       # rows not a whole number of sequences
     assert dec(rows=4096) == -1                        # cache rows beyond the head stride
     assert dec(pos0=2048) == -1                        # position outside the cache
     assert dec(R=2, pos0=2**31 - 1) == -1              # pos0 + R would wrap a 32-bit int
     assert dec(k=vp(0x1004)) == -2                     # cache not 16-byte aligned
+    assert dec(q=vp(0x1004)) == -2                     # q not 16-byte aligned (read with 16-byte loads)
+    assert dec(qhs=128 * 2 + 4) == -2                  # q head stride not a multiple of 8
     assert dec(R=0) == 0                               # no rows: no-op
 
 
