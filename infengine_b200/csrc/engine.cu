@@ -60,6 +60,8 @@ struct Engine {
   size_t split_ws_bytes = 0;
   std::vector<int> pos_host;
   long long step_host = 0;
+  // pinned staging of ie_engine_step's tokens in [0, B) and ids out [B, 2B)
+  int* h_tok = nullptr;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   // tensor parallelism (world == 1: single GPU)
@@ -184,6 +186,7 @@ void release(Engine* E) {
                   E->history, E->step,  E->chunk, E->ids,  E->lm_ws, E->part, E->keys, E->split_ws};
   for (void* p : bufs)
     if (p) cudaFree(p);
+  if (E->h_tok) cudaFreeHost(E->h_tok);
   if (E->own_stream && E->st) cudaStreamDestroy(E->st);
   delete E;
 }
@@ -275,6 +278,7 @@ int ie_engine_create_tp(ie_dtype dt, const ie_llama_desc* desc, int max_batch, i
   alloc(reinterpret_cast<void**>(&E->chunk), R * sizeof(int));
   alloc(reinterpret_cast<void**>(&E->ids), R * sizeof(int));
   alloc(&E->lm_ws, E->lm_ws_bytes);
+  if (ok) ok = cudaMallocHost(reinterpret_cast<void**>(&E->h_tok), 2 * max_batch * sizeof(int)) == cudaSuccess;
   if (E->max_rows > 16) {  // prefill chunks run the tensor-core kernels
     E->split_ws_bytes = ie_split_workspace_size();
     alloc(&E->split_ws, E->split_ws_bytes);
@@ -382,10 +386,13 @@ int ie_engine_step(ie_engine* eng, const int* tokens_in, int* tokens_out) {
     if (E.pos_host[b] + 1 > E.ctx) return IE_ERR_UNSUPPORTED;
   }
   IE_TRY(capture(E));
-  IE_TRY(check(cudaMemcpyAsync(E.tok_in, tokens_in, E.B * sizeof(int), cudaMemcpyHostToDevice, E.st)));
+  // the copies go through pinned staging, so both are plain DMA transfers
+  std::memcpy(E.h_tok, tokens_in, E.B * sizeof(int));
+  IE_TRY(check(cudaMemcpyAsync(E.tok_in, E.h_tok, E.B * sizeof(int), cudaMemcpyHostToDevice, E.st)));
   IE_TRY(check(cudaGraphLaunch(E.exec, E.st)));
-  IE_TRY(check(cudaMemcpyAsync(tokens_out, E.tok_in, E.B * sizeof(int), cudaMemcpyDeviceToHost, E.st)));
+  IE_TRY(check(cudaMemcpyAsync(E.h_tok + E.B, E.tok_in, E.B * sizeof(int), cudaMemcpyDeviceToHost, E.st)));
   IE_TRY(check(cudaStreamSynchronize(E.st)));
+  std::memcpy(tokens_out, E.h_tok + E.B, E.B * sizeof(int));
   E.step_host += 1;
   for (int b = 0; b < E.B; ++b) E.pos_host[b] += 1;
   return IE_OK;
