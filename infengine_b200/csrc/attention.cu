@@ -309,9 +309,13 @@ __global__ void __launch_bounds__(kFdThreads) decode_attention_kernel(const FdPa
     if (!fd_wait(fd_smem_u32(&bars[i % S]), (uint32_t)((i / S) & 1), &abort_s))
       atomicMin(&fail_at, i);
   };
+  // a slot that takes another chunk is refilled once every warp is done
+  // with it; the last S chunks free nothing, so warps run on through them
+  // without a barrier (the condition is the same for the whole CTA)
   auto next = [&](int i) {
-    __syncthreads();  // every warp is done with slot i % S
-    if (tid == 0 && !abort_s && i + S < total) issue(i + S);
+    if (i + S >= total) return;
+    __syncthreads();
+    if (tid == 0 && !abort_s) issue(i + S);
   };
 
   // ---- scores: S[row][head] = K[row] . q[head] over the low and the high
